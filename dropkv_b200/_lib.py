@@ -1,0 +1,89 @@
+"""ctypes binding of libdropkv_b200.so (the C ABI declared in include/dropkv_b200.h).
+
+The library is the only compute path of this package: if it is missing the
+first call raises, there is no Python or CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdropkv_b200.so")
+
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+ROUND_NONE, ROUND_BF16, ROUND_F16 = 0, 1, 2
+OK, ERR_ARG, ERR_WORKSPACE, ERR_CUDA, ERR_UNSUPPORTED, ERR_DEVICE = range(6)
+
+_c_int, _c_i64, _c_f, _c_sz, _c_p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "dropkv_version": (ctypes.c_char_p, []),
+    "dropkv_last_error": (ctypes.c_char_p, []),
+    "dropkv_launch_count": (ctypes.c_uint64, []),
+    "dropkv_scores_workspace_size": (_c_sz, [_c_int] * 6),
+    "dropkv_scores": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_int,
+                               _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int, _c_p,
+                               _c_p, _c_sz, _c_p]),
+    "dropkv_select_workspace_size": (_c_sz, [_c_int] * 3),
+    "dropkv_select": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_p,
+                               _c_sz, _c_p]),
+    "dropkv_gather": (_c_int, [_c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_int,
+                               _c_p, _c_p, _c_p]),
+    "dropkv_compress_workspace_size": (_c_sz, [_c_int] * 6),
+    "dropkv_compress": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_int,
+                                 _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int,
+                                 _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz,
+                                 _c_p]),
+}
+
+
+class DropKVError(RuntimeError):
+    """A C-ABI call returned an error status."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[dropkv_b200 status {code}] {message}")
+        self.code = code
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"dropkv_b200 CUDA library not found at {LIB_PATH}; build it with "
+                "`python -m dropkv_b200.build` (there is no fallback path)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != OK:
+        msg = load().dropkv_last_error().decode(errors="replace")
+        raise DropKVError(rc, f"{what}: {msg}" if what else msg)
+
+
+def launch_count() -> int:
+    """Kernel launches issued by the library so far in this process."""
+    return int(load().dropkv_launch_count())
+
+
+def version() -> str:
+    return load().dropkv_version().decode()

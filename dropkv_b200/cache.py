@@ -1,0 +1,389 @@
+"""DropKV KV cache with the CUDA eviction backend.
+
+Keeps the reference's interface and state machine (dropkv_cache.py:310-807) so it
+drops in: ``DropKVCache(keep_ratio, window_size, kernel_size, use_triton)``,
+``update`` (5-argument form and the HF 4-argument form), ``_compute_keep_indices``,
+``_gather_compressed``, ``get_seq_length``, ``get_mask_sizes`` and the
+``prefill_chunked`` helper with its three eviction strategies.
+
+What changes is the backend: every eviction runs ``dropkv_b200.ops`` (the C ABI of
+libdropkv_b200.so).  ``use_triton`` is accepted for signature compatibility and
+both values select the CUDA kernels -- there is no PyTorch or CPU scoring branch.
+The reference's PyTorch branch also served queries shorter than the window
+(dropkv_cache.py:399-407, scoring window min(window, Lq)); here the CUDA scorer
+takes that shorter window directly, and protection still covers ``window_size``
+positions (dropkv_cache.py:466-467).
+"""
+
+from __future__ import annotations
+
+import logging
+from collections.abc import Iterable
+from typing import Any, Optional
+
+import torch
+
+from . import ops
+
+logger = logging.getLogger(__name__)
+
+__all__ = ["Cache", "DynamicCache", "DropKVCache", "prefill_chunked"]
+
+
+class Cache:
+    """Minimal cache base (the interface of dropkv_cache.py:13-101)."""
+
+    is_compileable = False
+
+    def update(self, query_states, key_states, value_states, layer_idx, cache_kwargs=None):
+        raise NotImplementedError("Make sure to implement `update` in a subclass.")
+
+    def get_seq_length(self, layer_idx: Optional[int] = 0) -> int:
+        raise NotImplementedError("Make sure to implement `get_seq_length` in a subclass.")
+
+    def get_max_cache_shape(self) -> Optional[int]:
+        raise NotImplementedError("Make sure to implement `get_max_cache_shape` in a subclass.")
+
+    def get_usable_length(self, new_seq_length: int, layer_idx: Optional[int] = 0) -> int:
+        max_length = self.get_max_cache_shape()
+        previous = self.get_seq_length(layer_idx)
+        if max_length is not None and previous + new_seq_length > max_length:
+            return max_length - new_seq_length
+        return previous
+
+    def reorder_cache(self, beam_idx: torch.LongTensor):
+        for i in range(len(self.key_cache)):
+            if self.key_cache[i].numel():
+                self.key_cache[i] = self.key_cache[i].index_select(0, beam_idx.to(self.key_cache[i].device))
+            if self.value_cache[i].numel():
+                self.value_cache[i] = self.value_cache[i].index_select(0, beam_idx.to(self.value_cache[i].device))
+
+    @property
+    def seen_tokens(self):
+        return getattr(self, "_seen_tokens", None)
+
+    def get_mask_sizes(self, cache_position: torch.Tensor, layer_idx: int) -> tuple[int, int]:
+        return cache_position.shape[0] + self.get_seq_length(), 0
+
+
+class DynamicCache(Cache):
+    """List-of-tensors KV store, one [B, Hkv, L, D] pair per layer (dropkv_cache.py:104-307)."""
+
+    def __init__(self, _distributed_cache_data: Optional[Iterable] = None) -> None:
+        super().__init__()
+        self._seen_tokens = 0
+        self.key_cache: list[torch.Tensor] = []
+        self.value_cache: list[torch.Tensor] = []
+        if _distributed_cache_data is not None:
+            for k, v in _distributed_cache_data:
+                self.key_cache.append(k)
+                self.value_cache.append(v)
+
+    def __getitem__(self, layer_idx: int):
+        if layer_idx < len(self):
+            return self.key_cache[layer_idx], self.value_cache[layer_idx]
+        raise KeyError(f"Cache only has {len(self)} layers, attempted to access layer with index {layer_idx}")
+
+    def __iter__(self):
+        for i in range(len(self)):
+            yield self.key_cache[i], self.value_cache[i]
+
+    def __len__(self):
+        return len(self.key_cache)
+
+    def update(self, query_states, key_states, value_states, layer_idx, cache_kwargs=None):
+        if layer_idx == 0:
+            self._seen_tokens += key_states.shape[-2]
+        if key_states is not None:
+            if len(self.key_cache) <= layer_idx:
+                while len(self.key_cache) < layer_idx:
+                    self.key_cache.append(torch.tensor([]))
+                    self.value_cache.append(torch.tensor([]))
+                self.key_cache.append(key_states)
+                self.value_cache.append(value_states)
+            elif not self.key_cache[layer_idx].numel():
+                self.key_cache[layer_idx] = key_states
+                self.value_cache[layer_idx] = value_states
+            else:
+                self.key_cache[layer_idx] = torch.cat([self.key_cache[layer_idx], key_states], dim=-2)
+                self.value_cache[layer_idx] = torch.cat([self.value_cache[layer_idx], value_states], dim=-2)
+        return self.key_cache[layer_idx], self.value_cache[layer_idx]
+
+    def get_seq_length(self, layer_idx: Optional[int] = 0) -> int:
+        if len(self.key_cache) <= layer_idx or not self.key_cache[layer_idx].numel():
+            return 0
+        return self.key_cache[layer_idx].shape[-2]
+
+    def get_max_cache_shape(self) -> Optional[int]:
+        return None
+
+    def to_legacy_cache(self):
+        return tuple((self.key_cache[i], self.value_cache[i]) for i in range(len(self)))
+
+    @classmethod
+    def from_legacy_cache(cls, past_key_values=None):
+        cache = cls()
+        if past_key_values is not None:
+            for i, (k, v) in enumerate(past_key_values):
+                cache.update(None, k, v, i)
+        return cache
+
+    def crop(self, max_length: int):
+        if max_length < 0:
+            max_length = self.get_seq_length() - abs(max_length)
+        if self.get_seq_length() <= max_length:
+            return
+        self._seen_tokens = max_length
+        for i in range(len(self.key_cache)):
+            if self.key_cache[i].numel():
+                self.key_cache[i] = self.key_cache[i][..., :max_length, :]
+                self.value_cache[i] = self.value_cache[i][..., :max_length, :]
+
+    def batch_split(self, full_batch_size: int, split_size: int):
+        out = []
+        for i in range(0, full_batch_size, split_size):
+            c = DynamicCache()
+            c._seen_tokens = self._seen_tokens
+            c.key_cache = [t[i:i + split_size] for t in self.key_cache]
+            c.value_cache = [t[i:i + split_size] for t in self.value_cache]
+            out.append(c)
+        return out
+
+    @classmethod
+    def from_batch_splits(cls, splits, **kwargs):
+        cache = cls(**kwargs)
+        for i in range(len(splits[0])):
+            ks = [s.key_cache[i] for s in splits if s.key_cache[i].numel()]
+            vs = [s.value_cache[i] for s in splits if s.value_cache[i].numel()]
+            if ks:
+                cache.update(None, torch.cat(ks, dim=0), torch.cat(vs, dim=0), i)
+        return cache
+
+    def batch_repeat_interleave(self, repeats: int):
+        for i in range(len(self)):
+            self.key_cache[i] = self.key_cache[i].repeat_interleave(repeats, dim=0)
+            self.value_cache[i] = self.value_cache[i].repeat_interleave(repeats, dim=0)
+
+    def batch_select_indices(self, indices: torch.Tensor):
+        for i in range(len(self)):
+            self.key_cache[i] = self.key_cache[i][indices, ...]
+            self.value_cache[i] = self.value_cache[i][indices, ...]
+
+
+_VALID_MODES = ("single_pass", "accumulate", "evict_accumulated")
+
+
+class DropKVCache(DynamicCache):
+    """KV cache that evicts at prefill with the DropKV score (CUDA backend)."""
+
+    def __init__(self, keep_ratio: float = 0.1, window_size: int = 8, kernel_size: int = 11,
+                 use_triton: bool = True) -> None:
+        super().__init__()
+        if not 0 < keep_ratio <= 1.0:
+            raise ValueError(f"keep_ratio must be in (0, 1], got {keep_ratio}")
+        if window_size <= 0:
+            raise ValueError(f"window_size must be positive, got {window_size}")
+        if kernel_size < 1 or kernel_size % 2 == 0:
+            raise ValueError(f"kernel_size must be a positive odd integer, got {kernel_size}")
+        self.keep_ratio = keep_ratio
+        self.window_size = window_size
+        self.kernel_size = kernel_size
+        self.use_triton = use_triton  # accepted for compatibility; CUDA either way
+        # "single_pass" | "accumulate" | "evict_accumulated" (set by prefill_chunked)
+        self._prefill_mode = "single_pass"
+        self._evict_use_seen_tokens = False
+        self._budget_max_kv_tokens: Optional[int] = None
+
+    def batch_split(self, full_batch_size: int, split_size: int):
+        raise NotImplementedError(
+            "DropKVCache does not support batch_split (beam search). "
+            "Use DynamicCache for beam search or implement DropKV-aware splitting.")
+
+    @classmethod
+    def from_batch_splits(cls, splits, **kwargs):
+        raise NotImplementedError(
+            "DropKVCache does not support from_batch_splits (beam search). "
+            "Use DynamicCache for beam search or implement DropKV-aware merging.")
+
+    # -- eviction ---------------------------------------------------------------
+    def _keep_len(self, seq_len: int, total_tokens: Optional[int], max_keep_len: Optional[int]) -> int:
+        """dropkv_cache.py:470-473."""
+        base = total_tokens if total_tokens is not None else seq_len
+        kl = min(seq_len, max(int(self.keep_ratio * base), self.window_size, 1))
+        if max_keep_len is not None:
+            kl = min(kl, max_keep_len)
+        return kl
+
+    def _check_heads(self, query_states, key_states):
+        hq, hkv = query_states.shape[1], key_states.shape[1]
+        if hq % hkv != 0:
+            raise ValueError(f"Query heads {hq} must be divisible by KV heads {hkv}")
+
+    def _compute_keep_indices(self, query_states: torch.Tensor, key_states: torch.Tensor,
+                              value_states: torch.Tensor, total_tokens: Optional[int] = None,
+                              max_keep_len: Optional[int] = None) -> torch.Tensor:
+        """Sorted kept positions [B, Hkv, keep_len] int64 (dropkv_cache.py:355-477)."""
+        self._check_heads(query_states, key_states)
+        seq_len = key_states.shape[2]
+        W = min(self.window_size, query_states.shape[2])
+        sc = ops.scores(query_states, key_states.contiguous(), value_states.contiguous(), W)
+        kl = self._keep_len(seq_len, total_tokens, max_keep_len)
+        return ops.select_keep_indices(sc, self.kernel_size, self.window_size, kl)
+
+    @staticmethod
+    def _gather_compressed(key_states: torch.Tensor, value_states: torch.Tensor,
+                           keep_idx: torch.Tensor):
+        """dropkv_cache.py:479-491."""
+        return ops.gather_compressed(key_states, value_states, keep_idx)
+
+    def _evict(self, query_states, key_states, value_states):
+        """Fused _compute_keep_indices + _gather_compressed: one C-ABI call."""
+        self._check_heads(query_states, key_states)
+        total = self._seen_tokens if self._evict_use_seen_tokens else None
+        kl = self._keep_len(key_states.shape[2], total, self._budget_max_kv_tokens)
+        W = min(self.window_size, query_states.shape[2])
+        _, kc, vc = ops.compress(query_states, key_states, value_states, W, self.kernel_size, kl,
+                                 protect_window=self.window_size)
+        return kc, vc
+
+    # -- state machine (dropkv_cache.py:493-622) --------------------------------
+    def update(self, query_states, key_states, value_states, layer_idx, cache_kwargs: Optional[dict[str, Any]] = None):
+        # HF calls update(key, value, layer_idx, cache_kwargs): shift the arguments.
+        if isinstance(value_states, int) and isinstance(layer_idx, dict):
+            cache_kwargs = layer_idx
+            layer_idx = value_states
+            value_states = key_states
+            key_states = query_states
+            query_states = cache_kwargs.get("query_states") if cache_kwargs else None
+            if query_states is None:
+                logger.warning(
+                    "DropKVCache.update() called without query_states — eviction disabled for this "
+                    "layer. Patch your transformers to pass query_states in cache_kwargs.")
+
+        if layer_idx == 0:
+            self._seen_tokens += key_states.shape[-2]
+
+        n_layers = len(self.key_cache)
+        if n_layers < layer_idx:
+            raise ValueError("Use DynamicCache.")
+
+        if n_layers == layer_idx:  # first time this layer is seen: prefill
+            if query_states is None:
+                if self._prefill_mode != "single_pass":
+                    logger.warning("query_states is None at layer %d — storing full KV without eviction.", layer_idx)
+                self.key_cache.append(key_states)
+                self.value_cache.append(value_states)
+                return key_states, value_states
+            if self._prefill_mode not in _VALID_MODES:
+                raise ValueError(f"Invalid _prefill_mode: {self._prefill_mode!r}")
+            if self._prefill_mode == "accumulate" or key_states.shape[2] < self.window_size:
+                self.key_cache.append(key_states)
+                self.value_cache.append(value_states)
+                return key_states, value_states
+            kc, vc = self._evict(query_states, key_states, value_states)
+            self.key_cache.append(kc)
+            self.value_cache.append(vc)
+            return key_states, value_states
+
+        # continuation: decode or chunked prefill
+        mode = self._prefill_mode
+        if mode == "accumulate" or mode == "single_pass":
+            self.key_cache[layer_idx] = torch.cat([self.key_cache[layer_idx], key_states], dim=-2)
+            self.value_cache[layer_idx] = torch.cat([self.value_cache[layer_idx], value_states], dim=-2)
+            return self.key_cache[layer_idx], self.value_cache[layer_idx]
+        if mode == "evict_accumulated":
+            full_k = torch.cat([self.key_cache[layer_idx], key_states], dim=-2)
+            full_v = torch.cat([self.value_cache[layer_idx], value_states], dim=-2)
+            if query_states is not None and full_k.shape[2] >= self.window_size:
+                kc, vc = self._evict(query_states, full_k, full_v)
+                self.key_cache[layer_idx] = kc
+                self.value_cache[layer_idx] = vc
+            else:
+                self.key_cache[layer_idx] = full_k
+                self.value_cache[layer_idx] = full_v
+            return full_k, full_v
+        raise ValueError(f"Invalid _prefill_mode {mode!r} in decode path")
+
+    def get_seq_length(self, layer_idx: Optional[int] = 0) -> int:
+        """Logical length (tokens seen), used for RoPE positions after eviction."""
+        if len(self.key_cache) <= layer_idx:
+            return 0
+        return self._seen_tokens
+
+    def get_mask_sizes(self, cache_position: torch.Tensor, layer_idx: int = 0) -> tuple[int, int]:
+        """(stored KV length + query length, 0): the mask must match stored tensors."""
+        q = cache_position.shape[0]
+        empty = len(self.key_cache) <= layer_idx or not self.key_cache[layer_idx].numel()
+        stored = 0 if empty else self.key_cache[layer_idx].shape[-2]
+        return stored + q, 0
+
+
+def prefill_chunked(model, input_ids, cache, chunk_size=4096, evict_strategy="last_chunk",
+                    max_kv_tokens=32768, **forward_kwargs):
+    """Chunked prefill with DropKV eviction (dropkv_cache.py:651-807).
+
+    ``evict_strategy``: ``"last_chunk"`` (accumulate, evict on the last chunk),
+    ``"budget"`` (evict to keep_ratio * tokens seen whenever the stored KV would
+    exceed ``max_kv_tokens``, which also caps keep_len) or ``"every_chunk"``.
+    On any exception the cache is cleared; its mode flags are always restored.
+    """
+    if not isinstance(cache, DropKVCache):
+        raise TypeError(f"cache must be DropKVCache, got {type(cache).__name__}")
+    if len(cache.key_cache) > 0:
+        raise ValueError("prefill_chunked() requires a fresh (empty) cache. Create a new DropKVCache instance.")
+    if chunk_size < cache.window_size:
+        raise ValueError(f"chunk_size ({chunk_size}) must be >= window_size ({cache.window_size})")
+    bad = {"attention_mask", "position_ids", "cache_position"} & forward_kwargs.keys()
+    if bad:
+        raise ValueError(
+            f"prefill_chunked() does not support sequence-shaped kwargs {bad} — the model computes "
+            f"these internally per chunk. Remove them from forward_kwargs.")
+    strategies = ("last_chunk", "budget", "every_chunk")
+    if evict_strategy not in strategies:
+        raise ValueError(f"evict_strategy must be one of {strategies}, got {evict_strategy!r}")
+    if evict_strategy == "budget":
+        if max_kv_tokens is None:
+            raise ValueError("max_kv_tokens is required when evict_strategy='budget'")
+        if max_kv_tokens < cache.window_size:
+            raise ValueError(
+                f"max_kv_tokens ({max_kv_tokens}) must be >= window_size ({cache.window_size}) "
+                f"to preserve protected tail tokens")
+
+    B, L = input_ids.shape
+    if L <= chunk_size and evict_strategy == "last_chunk":
+        with torch.no_grad():
+            return model(input_ids, past_key_values=cache, use_cache=True, **forward_kwargs)
+
+    starts = list(range(0, L, chunk_size))
+    try:
+        cache._evict_use_seen_tokens = evict_strategy in ("budget", "every_chunk")
+        if evict_strategy == "budget":
+            cache._budget_max_kv_tokens = max_kv_tokens
+        with torch.no_grad():
+            output = None
+            for i, start in enumerate(starts):
+                end = min(start + chunk_size, L)
+                last = i == len(starts) - 1
+                if evict_strategy == "last_chunk":
+                    cache._prefill_mode = "evict_accumulated" if last else "accumulate"
+                elif evict_strategy == "every_chunk":
+                    cache._prefill_mode = "single_pass" if i == 0 else "evict_accumulated"
+                else:  # budget
+                    if last:
+                        cache._prefill_mode = "evict_accumulated"
+                    else:
+                        stored = cache.key_cache[0].shape[2] if cache.key_cache else 0
+                        cache._prefill_mode = ("evict_accumulated" if stored + (end - start) > max_kv_tokens
+                                               else "accumulate")
+                output = model(input_ids[:, start:end], past_key_values=cache, use_cache=True,
+                               **forward_kwargs)
+            return output
+    except BaseException:
+        cache.key_cache.clear()
+        cache.value_cache.clear()
+        cache._seen_tokens = 0
+        raise
+    finally:
+        cache._prefill_mode = "single_pass"
+        cache._evict_use_seen_tokens = False
+        cache._budget_max_kv_tokens = None

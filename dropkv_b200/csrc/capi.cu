@@ -1,0 +1,237 @@
+// extern "C" entry points of libdropkv_b200.so: argument checks, scratch
+// planning and the launch sequence of each public operation.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace dropkv {
+
+static thread_local std::string g_err;
+
+void set_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+}
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+static std::atomic<uint64_t> g_launches{0};
+
+int check_launch(const char* what, int launches) {
+  g_launches.fetch_add((uint64_t)launches, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return DROPKV_OK;
+}
+
+int num_sms_current_device() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 64 && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev < 64) cache[dev] = n;
+  return n;
+}
+
+int simt_max_splits();
+int simt_tile();
+
+ScorePlan plan_scores(int B, int Hkv, int Lk, int M, int D) {
+  ScorePlan p;
+  std::memset(&p, 0, sizeof(p));
+  p.BH = B * Hkv;
+  p.tile = simt_tile();
+  p.tiles = (Lk + p.tile - 1) / p.tile;
+  const int target = 2 * num_sms_current_device();
+  int s = (target + p.BH - 1) / p.BH;
+  s = std::min(s, std::max(1, p.tiles / 4));
+  s = std::min(s, simt_max_splits());
+  s = std::max(s, 1);
+  p.tps = (p.tiles + s - 1) / s;
+  p.splits = (p.tiles + p.tps - 1) / p.tps;  // no empty split
+  const size_t rows = (size_t)p.BH * p.splits * M;
+  size_t off = 0;
+  p.off_pm = off; off = align_up(off + rows * 4, 256);
+  p.off_ps = off; off = align_up(off + rows * 4, 256);
+  p.off_py = off; off = align_up(off + rows * D * 4, 256);
+  p.off_lse = off; off = align_up(off + (size_t)p.BH * M * 4, 256);
+  p.off_yn = off; off = align_up(off + (size_t)p.BH * M * 4, 256);
+  p.off_y = off; off = align_up(off + (size_t)p.BH * M * D * 4, 256);
+  p.bytes = off;
+  return p;
+}
+
+static bool d_supported(int D) { return D == 32 || D == 64 || D == 128 || D == 256; }
+
+static int elem_bytes_of(int dtype) {
+  switch (dtype) {
+    case DROPKV_DTYPE_F32: return 4;
+    case DROPKV_DTYPE_F16: return 2;
+    case DROPKV_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+static int check_score_args(const void* q, int Lq, const void* k, const void* v, int dtype, int B,
+                            int Hq, int Hkv, int Lk, int D, int window, int round_p) {
+  if (!q || !k || !v) return fail(DROPKV_ERR_ARG, "Q, K and V must be non-NULL device pointers");
+  if (!elem_bytes_of(dtype)) return fail(DROPKV_ERR_ARG, "unknown dtype %d", dtype);
+  if (B < 1 || Hq < 1 || Hkv < 1 || Lk < 1 || Lq < 1 || D < 1)
+    return fail(DROPKV_ERR_ARG, "all sizes must be positive (B=%d Hq=%d Hkv=%d Lq=%d Lk=%d D=%d)", B, Hq, Hkv, Lq, Lk, D);
+  if (Hq % Hkv != 0) return fail(DROPKV_ERR_ARG, "Hq (%d) must be divisible by Hkv (%d)", Hq, Hkv);
+  if (window < 1) return fail(DROPKV_ERR_ARG, "window_size must be a positive int, got %d", window);
+  if (Lq < window) return fail(DROPKV_ERR_ARG, "Lq (%d) must be >= window_size (%d)", Lq, window);
+  if (Lk < window) return fail(DROPKV_ERR_ARG, "Lk (%d) must be >= window_size (%d)", Lk, window);
+  if (Lq > Lk) return fail(DROPKV_ERR_ARG, "Lq (%d) must be <= Lk (%d) (Q must be tail-aligned suffix)", Lq, Lk);
+  if ((int64_t)B * Hkv > 65535) return fail(DROPKV_ERR_ARG, "B*Hkv (%lld) exceeds 65535", (long long)B * Hkv);
+  if (!d_supported(D)) return fail(DROPKV_ERR_UNSUPPORTED, "head_dim %d not supported (32, 64, 128, 256)", D);
+  if (round_p < DROPKV_ROUND_NONE || round_p > DROPKV_ROUND_F16) return fail(DROPKV_ERR_ARG, "bad round_p %d", round_p);
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % 16)
+    return fail(DROPKV_ERR_ARG, "K and V must be 16-byte aligned");
+  return DROPKV_OK;
+}
+
+static ScoreProblem make_problem(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd,
+                                 int Lq, const void* k, const void* v, int B, int Hq, int Hkv, int Lk,
+                                 int D, int window, float eps, int round_p, float* scores) {
+  ScoreProblem p;
+  p.q = q; p.q_sb = q_sb; p.q_sh = q_sh; p.q_ss = q_ss; p.q_sd = q_sd; p.Lq = Lq;
+  p.k = k; p.v = v; p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.Lk = Lk; p.D = D;
+  p.W = window; p.g = Hq / Hkv; p.M = p.g * window;
+  p.scale = (float)(1.0 / std::sqrt((double)D));
+  p.eps = eps; p.round_mode = round_p; p.scores = scores;
+  return p;
+}
+
+static int check_ws(void* ws, size_t have, size_t need) {
+  if (need == 0) return DROPKV_OK;
+  if (!ws) return fail(DROPKV_ERR_WORKSPACE, "workspace is NULL (%zu bytes needed)", need);
+  if (have < need) return fail(DROPKV_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", have, need);
+  if (reinterpret_cast<uintptr_t>(ws) % 256) return fail(DROPKV_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  return DROPKV_OK;
+}
+
+static int run_scores(const ScoreProblem& p, int dtype, void* ws, cudaStream_t st) {
+  ScorePlan plan = plan_scores(p.B, p.Hkv, p.Lk, p.M, p.D);
+  return launch_scores_simt(p, plan, ws, st, dtype);
+}
+
+static int check_select_args(int B, int Hkv, int Lk, int kernel_size, int protect, int keep_len) {
+  if (B < 1 || Hkv < 1 || Lk < 1) return fail(DROPKV_ERR_ARG, "B, Hkv and Lk must be positive");
+  if ((int64_t)B * Hkv > 2147483647) return fail(DROPKV_ERR_ARG, "B*Hkv too large");
+  if (kernel_size < 1 || kernel_size % 2 == 0)
+    return fail(DROPKV_ERR_ARG, "kernel_size must be a positive odd integer, got %d", kernel_size);
+  if (protect < 0) return fail(DROPKV_ERR_ARG, "protect window must be >= 0, got %d", protect);
+  if (keep_len < 1 || keep_len > Lk)
+    return fail(DROPKV_ERR_ARG, "keep_len must be in [1, Lk=%d], got %d", Lk, keep_len);
+  return DROPKV_OK;
+}
+
+}  // namespace dropkv
+
+using namespace dropkv;
+
+extern "C" {
+
+const char* dropkv_version(void) { return "dropkv_b200 0.1.0 (sm_100a)"; }
+
+const char* dropkv_last_error(void) { return g_err.c_str(); }
+
+uint64_t dropkv_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+size_t dropkv_scores_workspace_size(int B, int Hq, int Hkv, int Lk, int D, int window) {
+  if (B < 1 || Hq < 1 || Hkv < 1 || Lk < 1 || D < 1 || window < 1 || Hq % Hkv) return 0;
+  return plan_scores(B, Hkv, Lk, (Hq / Hkv) * window, D).bytes;
+}
+
+int dropkv_scores(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                  const void* k, const void* v, int dtype, int B, int Hq, int Hkv, int Lk, int D,
+                  int window, float eps, int round_p, float* scores, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  int rc = check_score_args(q, Lq, k, v, dtype, B, Hq, Hkv, Lk, D, window, round_p);
+  if (rc) return rc;
+  if (!scores) return fail(DROPKV_ERR_ARG, "scores must be a non-NULL device pointer");
+  size_t need = dropkv_scores_workspace_size(B, Hq, Hkv, Lk, D, window);
+  if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
+  ScoreProblem p = make_problem(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, B, Hq, Hkv, Lk, D, window, eps,
+                                round_p, scores);
+  return run_scores(p, dtype, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t dropkv_select_workspace_size(int B, int Hkv, int Lk) {
+  if (B < 1 || Hkv < 1 || Lk < 1) return 0;
+  return plan_select(B * Hkv, Lk).bytes;
+}
+
+int dropkv_select(const float* scores, int B, int Hkv, int Lk, int kernel_size, int protect_window,
+                  int keep_len, int64_t* keep_idx, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  int rc = check_select_args(B, Hkv, Lk, kernel_size, protect_window, keep_len);
+  if (rc) return rc;
+  if (!scores || !keep_idx) return fail(DROPKV_ERR_ARG, "scores and keep_idx must be non-NULL");
+  if ((rc = check_ws(workspace, workspace_bytes, dropkv_select_workspace_size(B, Hkv, Lk)))) return rc;
+  int protect = std::min(protect_window, Lk);
+  return launch_select(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, workspace,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dropkv_gather(const void* k, const void* v, int elem_bytes, int B, int Hkv, int Lk, int D,
+                  const int64_t* keep_idx, int keep_len, void* k_out, void* v_out, void* stream) {
+  if (!k || !v || !keep_idx || !k_out || !v_out) return fail(DROPKV_ERR_ARG, "NULL pointer argument");
+  if (elem_bytes != 2 && elem_bytes != 4) return fail(DROPKV_ERR_ARG, "elem_bytes must be 2 or 4");
+  if (B < 1 || Hkv < 1 || Lk < 1 || D < 1 || keep_len < 0)
+    return fail(DROPKV_ERR_ARG, "invalid gather sizes");
+  if ((int64_t)B * Hkv > 65535) return fail(DROPKV_ERR_ARG, "B*Hkv exceeds 65535");
+  return launch_gather(k, v, elem_bytes, B * Hkv, Lk, D, keep_idx, keep_len, k_out, v_out,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t dropkv_compress_workspace_size(int B, int Hq, int Hkv, int Lk, int D, int window) {
+  size_t s = dropkv_scores_workspace_size(B, Hq, Hkv, Lk, D, window);
+  if (!s) return 0;
+  size_t sc = align_up((size_t)B * Hkv * Lk * 4, 256);
+  return s + sc + dropkv_select_workspace_size(B, Hkv, Lk);
+}
+
+int dropkv_compress(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                    const void* k, const void* v, int dtype, int B, int Hq, int Hkv, int Lk, int D,
+                    int window, float eps, int round_p, int kernel_size, int protect_window,
+                    int keep_len, float* scores_out, int64_t* keep_idx, void* k_out, void* v_out,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_score_args(q, Lq, k, v, dtype, B, Hq, Hkv, Lk, D, window, round_p);
+  if (rc) return rc;
+  if ((rc = check_select_args(B, Hkv, Lk, kernel_size, protect_window, keep_len))) return rc;
+  if (!keep_idx || !k_out || !v_out) return fail(DROPKV_ERR_ARG, "keep_idx, k_out and v_out must be non-NULL");
+  size_t s_ws = dropkv_scores_workspace_size(B, Hq, Hkv, Lk, D, window);
+  size_t need = dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, window);
+  if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
+  char* base = reinterpret_cast<char*>(workspace);
+  float* scores = scores_out ? scores_out : reinterpret_cast<float*>(base + s_ws);
+  void* sel_ws = base + s_ws + align_up((size_t)B * Hkv * Lk * 4, 256);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ScoreProblem p = make_problem(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, B, Hq, Hkv, Lk, D, window, eps,
+                                round_p, scores);
+  if ((rc = run_scores(p, dtype, workspace, st))) return rc;
+  int protect = std::min(protect_window, Lk);
+  if ((rc = launch_select(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, sel_ws, st))) return rc;
+  return launch_gather(k, v, elem_bytes_of(dtype), B * Hkv, Lk, D, keep_idx, keep_len, k_out, v_out, st);
+}
+
+}  // extern "C"

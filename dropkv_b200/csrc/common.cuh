@@ -1,0 +1,104 @@
+// Shared device helpers and host-side plumbing for the dropkv_b200 kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/dropkv_b200.h"
+
+namespace dropkv {
+
+// ---------------------------------------------------------------------------
+// Error reporting (per host thread)
+// ---------------------------------------------------------------------------
+void set_error(const char* fmt, ...);
+int fail(int code, const char* fmt, ...);
+int check_launch(const char* what, int launches = 1);
+
+// ---------------------------------------------------------------------------
+// Element conversion
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float to_f(T x);
+template <>
+__device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// p rounded to the input dtype and widened back (torch's .to(dtype).float()).
+__device__ __forceinline__ float round_p(float p, int mode) {
+  if (mode == DROPKV_ROUND_BF16) return __bfloat162float(__float2bfloat16_rn(p));
+  if (mode == DROPKV_ROUND_F16) return __half2float(__float2half_rn(p));
+  return p;
+}
+
+// Float -> uint32 with unsigned order == float order; -0.0 maps like +0.0.
+__device__ __forceinline__ uint32_t ordered_key(float f) {
+  f = f + 0.0f;
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_to_float(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// ---------------------------------------------------------------------------
+// Score problem description (host + device)
+// ---------------------------------------------------------------------------
+struct ScoreProblem {
+  const void* q;
+  int64_t q_sb, q_sh, q_ss, q_sd;
+  int Lq;
+  const void* k;
+  const void* v;
+  int B, Hq, Hkv, Lk, D;
+  int W;       // query rows per head used (window)
+  int g;       // Hq / Hkv
+  int M;       // g * W
+  float scale; // 1 / sqrt(D)
+  float eps;
+  int round_mode;
+  float* scores;  // [B*Hkv, Lk]
+};
+
+// Scratch layout of the split-K scorer (fp32 regions, 256-byte aligned).
+struct ScorePlan {
+  int BH;
+  int tile;     // keys per split tile
+  int tiles;    // ceil(Lk / tile)
+  int splits;   // split-K factor
+  int tps;      // tiles per split
+  size_t off_pm, off_ps, off_py, off_lse, off_yn, off_y;
+  size_t bytes;
+};
+
+int num_sms_current_device();
+ScorePlan plan_scores(int B, int Hkv, int Lk, int M, int D);
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Launchers implemented per translation unit.
+int launch_scores_simt(const ScoreProblem& p, const ScorePlan& plan, void* ws, cudaStream_t st,
+                       int dtype);
+
+struct SelectPlan {
+  size_t off_keys;   // uint32 [BH, Lk]
+  size_t bytes;
+};
+SelectPlan plan_select(int BH, int Lk);
+int launch_select(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
+                  int64_t* keep_idx, void* ws, cudaStream_t st);
+int launch_gather(const void* k, const void* v, int elem_bytes, int BH, int Lk, int D,
+                  const int64_t* keep_idx, int keep_len, void* k_out, void* v_out,
+                  cudaStream_t st);
+
+}  // namespace dropkv

@@ -1,0 +1,239 @@
+"""Tensor-level operations over the C ABI (torch supplies memory and streams).
+
+* ``dropkv_scores_cuda`` -- drop-in for ``dropkv_scores_triton``
+  (dropkv_triton.py:643-828): same signature, same precondition checks with the same
+  ``AssertionError`` messages (dropkv_triton.py:679-707), same output.
+* ``scores``             -- the unguarded scorer used by the cache (also takes fp32
+  and windows shorter than the requested one, which the reference handles in its
+  PyTorch branch, dropkv_cache.py:401-460).
+* ``select_keep_indices`` -- pool + protect + top-k + sort (dropkv_cache.py:462-477).
+* ``gather_compressed``  -- dropkv_cache.py:479-491.
+* ``compress``           -- the whole path in one C call.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float32: _lib.DTYPE_F32, torch.float16: _lib.DTYPE_F16,
+               torch.bfloat16: _lib.DTYPE_BF16}
+_ROUND_CODE = {torch.float32: _lib.ROUND_NONE, torch.float16: _lib.ROUND_F16,
+               torch.bfloat16: _lib.ROUND_BF16}
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("dropkv_b200 runs on CUDA tensors only (no CPU path); got a "
+                               f"tensor on {t.device}")
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    # caching-allocator blocks are 512-byte aligned, above the 256 bytes the C ABI asks
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def scores(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int, eps: float = 1e-6,
+           round_p: bool = True) -> torch.Tensor:
+    """fp32 scores [B, Hkv, Lk] from the last ``window`` rows of Q.
+
+    ``round_p`` rounds p to the input dtype before the weight (the
+    ``match_pytorch_precision`` behaviour, dropkv_triton.py:584-587); it is a no-op
+    for fp32 inputs.  K and V must be contiguous; Q may have any strides.
+    """
+    _require_cuda(Q, K, V)
+    B, Hq, Lq, D = Q.shape
+    _, Hkv, Lk, _ = K.shape
+    dt = _DTYPE_CODE.get(Q.dtype)
+    if dt is None or K.dtype != Q.dtype or V.dtype != Q.dtype:
+        raise TypeError(f"Q, K, V must share one of fp32/fp16/bf16; got {Q.dtype}, {K.dtype}, {V.dtype}")
+    if not (K.is_contiguous() and V.is_contiguous()):
+        raise ValueError("K and V must be contiguous")
+    lib = _lib.load()
+    dev = Q.device
+    with torch.cuda.device(dev):
+        out = torch.empty(B, Hkv, Lk, dtype=torch.float32, device=dev)
+        nws = lib.dropkv_scores_workspace_size(B, Hq, Hkv, Lk, D, int(window))
+        ws = _workspace(nws, dev)
+        rc = lib.dropkv_scores(Q.data_ptr(), *Q.stride(), Lq, K.data_ptr(), V.data_ptr(), dt,
+                               B, Hq, Hkv, Lk, D, int(window), float(eps),
+                               _ROUND_CODE[Q.dtype] if round_p else _lib.ROUND_NONE,
+                               out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
+        _lib.check(rc, "dropkv_scores")
+    return out
+
+
+def dropkv_scores_cuda(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window_size: int = 8,
+                       eps: float = 1e-6, allow_tf32: bool = True,
+                       match_pytorch_precision: bool = True) -> torch.Tensor:
+    """Drop-in replacement of ``dropkv_scores_triton`` (dropkv_triton.py:643-828).
+
+    Same arguments and preconditions; ``allow_tf32`` is accepted for signature
+    compatibility (y is always accumulated in fp32 here, never TF32-rounded).
+    Returns scores [B, Hkv, Lk] fp32.
+    """
+    B, Hq, Lq, D = Q.shape
+    Hkv = K.shape[1]
+    Lk = K.shape[2]
+    # Preconditions and messages of dropkv_triton.py:679-707.
+    assert isinstance(window_size, int) and window_size > 0, (
+        f"window_size must be a positive int, got {window_size}")
+    assert Lq >= window_size, f"Lq ({Lq}) must be >= window_size ({window_size})"
+    assert Lk >= window_size, f"Lk ({Lk}) must be >= window_size ({window_size})"
+    assert Lq <= Lk, f"Lq ({Lq}) must be <= Lk ({Lk}) (Q must be tail-aligned suffix)"
+    assert Hq % Hkv == 0, f"Hq ({Hq}) must be divisible by Hkv ({Hkv})"
+    assert Q.is_cuda, "Inputs must be on CUDA"
+    assert Q.device == K.device == V.device, "All inputs must be on same device"
+    assert K.is_contiguous() and V.is_contiguous(), (
+        "K and V must be contiguous (Q is sliced internally)")
+    assert Q.dtype == K.dtype == V.dtype, "All inputs must have same dtype"
+    assert Q.dtype in (torch.float16, torch.bfloat16), (
+        f"Input dtype must be fp16 or bf16, got {Q.dtype}")
+    assert K.shape == V.shape, f"K and V shape mismatch: K={K.shape}, V={V.shape}"
+    assert K.shape[0] == B and K.shape[3] == D, (
+        f"K batch/head_dim mismatch: expected B={B}, D={D}, got K={K.shape}")
+    return scores(Q, K, V, window_size, eps, round_p=match_pytorch_precision)
+
+
+def select_keep_indices(scores_: torch.Tensor, kernel_size: int, protect_window: int,
+                        keep_len: int) -> torch.Tensor:
+    """keep_idx [B, Hkv, keep_len] int64 ascending (dropkv_cache.py:464-475)."""
+    _require_cuda(scores_)
+    if scores_.dtype != torch.float32:
+        raise TypeError("scores must be float32")
+    s = scores_.contiguous()
+    B, Hkv, Lk = s.shape
+    lib = _lib.load()
+    dev = s.device
+    with torch.cuda.device(dev):
+        idx = torch.empty(B, Hkv, keep_len, dtype=torch.int64, device=dev)
+        ws = _workspace(lib.dropkv_select_workspace_size(B, Hkv, Lk), dev)
+        rc = lib.dropkv_select(s.data_ptr(), B, Hkv, Lk, int(kernel_size), int(protect_window),
+                               int(keep_len), idx.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
+        _lib.check(rc, "dropkv_select")
+    return idx
+
+
+def gather_compressed(K: torch.Tensor, V: torch.Tensor, keep_idx: torch.Tensor):
+    """(K_c, V_c) = rows ``keep_idx`` of K and V along dim 2 (dropkv_cache.py:479-491)."""
+    _require_cuda(K, V, keep_idx)
+    K = K.contiguous()
+    V = V.contiguous()
+    if K.shape != V.shape or K.dtype != V.dtype:
+        raise ValueError("K and V must have the same shape and dtype")
+    idx = keep_idx.to(torch.int64).contiguous()
+    B, Hkv, Lk, D = K.shape
+    kl = idx.shape[-1]
+    if tuple(idx.shape[:2]) != (B, Hkv):
+        raise ValueError(f"keep_idx shape {tuple(idx.shape)} does not match K {tuple(K.shape)}")
+    Kc = torch.empty(B, Hkv, kl, D, dtype=K.dtype, device=K.device)
+    Vc = torch.empty_like(Kc)
+    if kl == 0:
+        return Kc, Vc
+    lib = _lib.load()
+    with torch.cuda.device(K.device):
+        rc = lib.dropkv_gather(K.data_ptr(), V.data_ptr(), K.element_size(), B, Hkv, Lk, D,
+                               idx.data_ptr(), kl, Kc.data_ptr(), Vc.data_ptr(), _stream(K.device))
+        _lib.check(rc, "dropkv_gather")
+    return Kc, Vc
+
+
+def compress(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int, kernel_size: int,
+             keep_len: int, protect_window: int | None = None, eps: float = 1e-6,
+             round_p: bool = True, return_scores: bool = False):
+    """scores -> pool/protect -> top-k -> sort -> gather in one C call.
+
+    Returns (keep_idx, K_c, V_c) and, with ``return_scores``, the raw scores too.
+    ``window`` is the scoring window (rows of Q used); ``protect_window`` the number
+    of newest positions forced into the kept set (defaults to ``window``).
+    """
+    _require_cuda(Q, K, V)
+    B, Hq, Lq, D = Q.shape
+    _, Hkv, Lk, _ = K.shape
+    dt = _DTYPE_CODE.get(Q.dtype)
+    if dt is None or K.dtype != Q.dtype or V.dtype != Q.dtype:
+        raise TypeError(f"Q, K, V must share one of fp32/fp16/bf16; got {Q.dtype}, {K.dtype}, {V.dtype}")
+    K = K.contiguous()
+    V = V.contiguous()
+    pw = window if protect_window is None else protect_window
+    lib = _lib.load()
+    dev = Q.device
+    with torch.cuda.device(dev):
+        idx = torch.empty(B, Hkv, keep_len, dtype=torch.int64, device=dev)
+        Kc = torch.empty(B, Hkv, keep_len, D, dtype=K.dtype, device=dev)
+        Vc = torch.empty_like(Kc)
+        sc = torch.empty(B, Hkv, Lk, dtype=torch.float32, device=dev) if return_scores else None
+        ws = _workspace(lib.dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, int(window)), dev)
+        rc = lib.dropkv_compress(Q.data_ptr(), *Q.stride(), Lq, K.data_ptr(), V.data_ptr(), dt,
+                                 B, Hq, Hkv, Lk, D, int(window), float(eps),
+                                 _ROUND_CODE[Q.dtype] if round_p else _lib.ROUND_NONE,
+                                 int(kernel_size), int(pw), int(keep_len),
+                                 sc.data_ptr() if sc is not None else None,
+                                 idx.data_ptr(), Kc.data_ptr(), Vc.data_ptr(),
+                                 ws.data_ptr(), ws.numel(), _stream(dev))
+        _lib.check(rc, "dropkv_compress")
+    if return_scores:
+        return idx, Kc, Vc, sc
+    return idx, Kc, Vc
+
+
+def inv_sqrt_d(D: int) -> float:
+    return 1.0 / math.sqrt(D)
+
+
+class Compressor:
+    """Pre-planned ``compress`` for a fixed problem shape.
+
+    Holds the outputs (keep_idx, K_c, V_c, optionally scores) and the scratch
+    workspace, so ``run`` issues exactly one C-ABI call and allocates nothing --
+    suitable for timing loops and CUDA-graph capture.
+    """
+
+    def __init__(self, B: int, Hq: int, Hkv: int, Lq: int, Lk: int, D: int, dtype: torch.dtype,
+                 window: int, kernel_size: int, keep_len: int, protect_window: int | None = None,
+                 eps: float = 1e-6, round_p: bool = True, keep_scores: bool = False,
+                 device="cuda"):
+        self.shape = (B, Hq, Hkv, Lq, Lk, D)
+        self.dtype = dtype
+        self.window = int(window)
+        self.kernel_size = int(kernel_size)
+        self.keep_len = int(keep_len)
+        self.protect = int(window if protect_window is None else protect_window)
+        self.eps = float(eps)
+        self.round = _ROUND_CODE[dtype] if round_p else _lib.ROUND_NONE
+        self.device = torch.device(device)
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            self.keep_idx = torch.empty(B, Hkv, keep_len, dtype=torch.int64, device=self.device)
+            self.k_out = torch.empty(B, Hkv, keep_len, D, dtype=dtype, device=self.device)
+            self.v_out = torch.empty_like(self.k_out)
+            self.scores = (torch.empty(B, Hkv, Lk, dtype=torch.float32, device=self.device)
+                           if keep_scores else None)
+            self.workspace = _workspace(
+                lib.dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, self.window), self.device)
+
+    def run(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, stream: int | None = None):
+        B, Hq, Hkv, Lq, Lk, D = self.shape
+        if tuple(Q.shape) != (B, Hq, Lq, D) or tuple(K.shape) != (B, Hkv, Lk, D) or K.shape != V.shape:
+            raise ValueError("input shapes do not match this Compressor")
+        if not (K.is_contiguous() and V.is_contiguous()):
+            raise ValueError("K and V must be contiguous")
+        lib = _lib.load()
+        st = _stream(self.device) if stream is None else stream
+        rc = lib.dropkv_compress(Q.data_ptr(), *Q.stride(), Lq, K.data_ptr(), V.data_ptr(),
+                                 _DTYPE_CODE[self.dtype], B, Hq, Hkv, Lk, D, self.window, self.eps,
+                                 self.round, self.kernel_size, self.protect, self.keep_len,
+                                 self.scores.data_ptr() if self.scores is not None else None,
+                                 self.keep_idx.data_ptr(), self.k_out.data_ptr(),
+                                 self.v_out.data_ptr(), self.workspace.data_ptr(),
+                                 self.workspace.numel(), st)
+        _lib.check(rc, "dropkv_compress")
+        return self.keep_idx, self.k_out, self.v_out

@@ -1,0 +1,118 @@
+/*
+ * dropkv_b200 -- C ABI of the B200-native DropKV prefill eviction path.
+ *
+ * The path scores every cached key position of every (sequence, KV head) by how
+ * much dropping it would perturb the attention output of the last `window`
+ * queries, max-pools the scores, protects the newest positions, keeps the top
+ * `keep_len` positions per head and compacts their K/V rows.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor pointers are CUDA device pointers on the current device.
+ *   - K and V are contiguous [B, Hkv, Lk, D]; Q is [B, Hq, Lq, D] with arbitrary
+ *     element strides (only its last `window` rows are read).  Q is tail-aligned:
+ *     query row Lq-1 corresponds to key position Lk-1.
+ *   - Query head h belongs to KV head h / (Hq / Hkv) (contiguous GQA groups).
+ *   - `dtype` is one of DROPKV_DTYPE_*; Q, K and V share it.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call only
+ *     enqueues work; nothing synchronises the host.
+ *   - Scratch memory is passed in by the caller (`workspace`, at least the size the
+ *     matching *_workspace_size function returns, 256-byte aligned).
+ *   - Return value: DROPKV_OK or an error code; dropkv_last_error() returns a
+ *     message for the calling host thread.  Kernels never trap.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   dropkv_scores          <- dropkv_triton.py:643-828  dropkv_scores_triton
+ *   dropkv_select          <- dropkv_cache.py:462-477   max_pool1d + protect + topk + sort
+ *   dropkv_gather          <- dropkv_cache.py:479-491   DropKVCache._gather_compressed
+ *   dropkv_compress        <- dropkv_cache.py:355-491   _compute_keep_indices + _gather_compressed
+ *   dropkv_compress_varlen <- dropkv_cache.py:355-491   the same, over a ragged list of heads
+ */
+#ifndef DROPKV_B200_H
+#define DROPKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DROPKV_API __attribute__((visibility("default")))
+#else
+#define DROPKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  DROPKV_DTYPE_F32 = 0,
+  DROPKV_DTYPE_F16 = 1,
+  DROPKV_DTYPE_BF16 = 2
+};
+
+enum {
+  DROPKV_OK = 0,
+  DROPKV_ERR_ARG = 1,         /* invalid shape, dtype, window, alignment ... */
+  DROPKV_ERR_WORKSPACE = 2,   /* workspace pointer NULL / too small / misaligned */
+  DROPKV_ERR_CUDA = 3,        /* a CUDA runtime call or launch failed */
+  DROPKV_ERR_UNSUPPORTED = 4, /* valid request this build has no kernel for (e.g. D) */
+  DROPKV_ERR_DEVICE = 5       /* a kernel reported a device-side status */
+};
+
+/* Round p to the input dtype before the weight (dropkv_triton.py:584-587). */
+enum { DROPKV_ROUND_NONE = 0, DROPKV_ROUND_BF16 = 1, DROPKV_ROUND_F16 = 2 };
+
+DROPKV_API const char* dropkv_version(void);
+DROPKV_API const char* dropkv_last_error(void);
+
+/* Number of kernel launches this library has issued in this process (all
+ * devices, all threads); lets a harness count the launches of a timed region. */
+DROPKV_API uint64_t dropkv_launch_count(void);
+
+/* Scratch bytes dropkv_scores needs for this problem on the current device.
+ * Replaces the intermediates allocated at dropkv_triton.py:736-769. */
+DROPKV_API size_t dropkv_scores_workspace_size(int B, int Hq, int Hkv, int Lk, int D, int window);
+
+/* scores[B, Hkv, Lk] (fp32) = DropKV eviction scores.
+ * Replaces dropkv_triton.py:643-828 (dropkv_scores_triton: Q window slice,
+ * Kernel A / split-A + C, Kernel B).  `window` is the number of query rows used
+ * (1 <= window <= Lq <= Lk), `eps` the weight constant, `round_p` one of
+ * DROPKV_ROUND_*.  q_s* are Q's element strides. */
+DROPKV_API int dropkv_scores(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                  const void* k, const void* v, int dtype, int B, int Hq, int Hkv, int Lk, int D,
+                  int window, float eps, int round_p, float* scores,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes dropkv_select needs. */
+DROPKV_API size_t dropkv_select_workspace_size(int B, int Hkv, int Lk);
+
+/* keep_idx[B, Hkv, keep_len] (int64, ascending) = top-keep_len positions of
+ * max_pool1d(scores, kernel_size, pad kernel_size/2, stride 1) after the last
+ * min(protect_window, Lk) positions are set to amax + 1.  Ties are broken towards
+ * the lower index.  Replaces dropkv_cache.py:464-475. */
+DROPKV_API int dropkv_select(const float* scores, int B, int Hkv, int Lk, int kernel_size, int protect_window,
+                  int keep_len, int64_t* keep_idx, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* k_out/v_out[B, Hkv, keep_len, D] = rows keep_idx of K/V (bit-exact copy).
+ * elem_bytes is 2 or 4.  Replaces dropkv_cache.py:479-491. */
+DROPKV_API int dropkv_gather(const void* k, const void* v, int elem_bytes, int B, int Hkv, int Lk, int D,
+                  const int64_t* keep_idx, int keep_len, void* k_out, void* v_out, void* stream);
+
+/* Scratch bytes dropkv_compress needs. */
+DROPKV_API size_t dropkv_compress_workspace_size(int B, int Hq, int Hkv, int Lk, int D, int window);
+
+/* The whole path in one call: scores -> pool/protect -> top-k -> sort -> gather.
+ * scores_out may be NULL (scores then live in the workspace).  Replaces the
+ * composition at dropkv_cache.py:355-491 (_compute_keep_indices followed by
+ * _gather_compressed). */
+DROPKV_API int dropkv_compress(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                    const void* k, const void* v, int dtype, int B, int Hq, int Hkv, int Lk, int D,
+                    int window, float eps, int round_p, int kernel_size, int protect_window,
+                    int keep_len, float* scores_out, int64_t* keep_idx, void* k_out, void* v_out,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DROPKV_B200_H */

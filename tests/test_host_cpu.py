@@ -1,0 +1,192 @@
+"""Host-side logic that needs no GPU: the C ABI library's exports, the wrapper's
+precondition checks (same AssertionError texts as dropkv_triton.py:679-707), the
+cache state machine paths that do not evict, and prefill_chunked's validation and
+cleanup (the reference's fake-model tests, tests/test_dropkv_triton.py:845-1331)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import dropkv_b200
+from dropkv_b200 import DropKVCache, _lib, ops, prefill_chunked
+from dropkv_b200.workloads import keep_len_rule
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    hdr = open(os.path.join(ROOT, "include", "dropkv_b200.h")).read()
+    return sorted(set(re.findall(r"DROPKV_API\s+[\w\s\*]+?\b(dropkv_\w+)\s*\(", hdr)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    syms = _declared_symbols()
+    assert len(syms) >= 9
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for s in syms:
+        assert hasattr(lib, s), f"{s} declared in include/dropkv_b200.h but not exported"
+    assert set(syms) <= set(_lib.SIGNATURES), "ctypes binding misses a declared symbol"
+    assert dropkv_b200.version().startswith("dropkv_b200")
+
+
+def test_workspace_queries_without_gpu():
+    lib = _lib.load()
+    n = lib.dropkv_scores_workspace_size(1, 32, 8, 32768, 128, 8)
+    assert n > 0 and n % 256 == 0
+    assert lib.dropkv_select_workspace_size(1, 8, 32768) >= 8 * 32768 * 4
+    assert lib.dropkv_compress_workspace_size(1, 32, 8, 32768, 128, 8) > n
+    assert lib.dropkv_scores_workspace_size(1, 7, 2, 100, 128, 8) == 0  # Hq % Hkv != 0
+
+
+def test_c_abi_rejects_bad_arguments_without_touching_the_gpu():
+    lib = _lib.load()
+    rc = lib.dropkv_scores(None, 0, 0, 0, 0, 8, None, None, 2, 1, 32, 8, 64, 128, 8, 1e-6, 1,
+                           None, None, 0, None)
+    assert rc == _lib.ERR_ARG
+    assert "non-NULL" in lib.dropkv_last_error().decode()
+    rc = lib.dropkv_select(None, 1, 8, 100, 10, 8, 10, None, None, 0, None)
+    assert rc == _lib.ERR_ARG and "odd" in lib.dropkv_last_error().decode()
+    rc = lib.dropkv_select(None, 1, 8, 100, 11, 8, 101, None, None, 0, None)
+    assert rc == _lib.ERR_ARG and "keep_len" in lib.dropkv_last_error().decode()
+
+
+def _mk(B=1, Hq=32, Hkv=8, Lq=64, Lk=64, D=128, dtype=torch.bfloat16):
+    return (torch.randn(B, Hq, Lq, D).to(dtype), torch.randn(B, Hkv, Lk, D).to(dtype),
+            torch.randn(B, Hkv, Lk, D).to(dtype))
+
+
+@pytest.mark.parametrize("kw,shape,match", [
+    (dict(window_size=0), {}, "positive int"),
+    ({}, dict(Lq=4, Lk=4), "must be >= window_size"),
+    ({}, dict(Lq=4, Lk=256), r"Lq.*must be >= window_size"),
+    ({}, dict(Lq=64, Lk=4), r"Lk.*must be >= window_size"),
+    ({}, dict(Lq=512, Lk=64), r"Lq.*must be <= Lk"),
+    ({}, dict(Hq=7, Hkv=4), "divisible"),
+    ({}, {}, "CUDA"),
+])
+def test_scores_guards_match_reference(kw, shape, match):
+    Q, K, V = _mk(**shape)
+    with pytest.raises(AssertionError, match=match):
+        ops.dropkv_scores_cuda(Q, K, V, **kw)
+
+
+def test_product_path_refuses_cpu_tensors():
+    Q, K, V = _mk()
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.scores(Q, K, V, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.compress(Q, K, V, 8, 11, 16)
+
+
+def test_keep_len_rule_matches_reference_arithmetic():
+    assert keep_len_rule(128, 0.3, 8) == 38
+    assert keep_len_rule(128, 0.3, 8, total_tokens=512) == 128
+    assert keep_len_rule(128, 0.3, 8, total_tokens=200) == 60
+    assert keep_len_rule(64, 0.01, 8, total_tokens=10) == 8
+    assert keep_len_rule(512, 0.8, 8, max_keep_len=100) == 100
+    c = DropKVCache(keep_ratio=0.3, window_size=8)
+    assert c._keep_len(128, None, None) == 38 and c._keep_len(128, 200, None) == 60
+
+
+def test_constructor_validation():
+    with pytest.raises(ValueError, match="keep_ratio"):
+        DropKVCache(keep_ratio=0.0)
+    with pytest.raises(ValueError, match="window_size"):
+        DropKVCache(window_size=0)
+    with pytest.raises(ValueError, match="kernel_size"):
+        DropKVCache(kernel_size=4)
+    with pytest.raises(NotImplementedError):
+        DropKVCache().batch_split(2, 1)
+
+
+def test_state_machine_paths_without_eviction():
+    Q, K, V = _mk(Lq=64, Lk=64)
+    c = DropKVCache(keep_ratio=0.3)
+    c._prefill_mode = "accumulate"
+    c.update(Q[:, :, :32], K[:, :, :32], V[:, :, :32], layer_idx=0)
+    assert c.key_cache[0].shape[2] == 32 and c._seen_tokens == 32
+    c.update(Q[:, :, 32:], K[:, :, 32:], V[:, :, 32:], layer_idx=0)
+    assert c.key_cache[0].shape[2] == 64 and c._seen_tokens == 64
+    # HF 4-arg call without query_states: stored in full
+    c2 = DropKVCache()
+    c2.update(K, V, 0, {"sin": None})
+    assert c2.key_cache[0].shape[2] == 64
+    # sequence shorter than the window: stored in full
+    c3 = DropKVCache(window_size=16)
+    c3.update(Q[:, :, :8], K[:, :, :8], V[:, :, :8], layer_idx=0)
+    assert c3.key_cache[0].shape[2] == 8
+    # skipped layer index
+    with pytest.raises(ValueError, match="Use DynamicCache"):
+        DropKVCache().update(Q, K, V, layer_idx=2)
+
+
+def test_invalid_modes_raise():
+    Q, K, V = _mk(Lq=8, Lk=8)
+    c = DropKVCache(window_size=16)
+    c._prefill_mode = "typo_mode"
+    with pytest.raises(ValueError, match="Invalid _prefill_mode"):
+        c.update(Q, K, V, layer_idx=0)
+    c = DropKVCache()
+    c._prefill_mode = "accumulate"
+    c.update(Q, K, V, layer_idx=0)
+    c._prefill_mode = "bogus"
+    with pytest.raises(ValueError, match="Invalid _prefill_mode"):
+        c.update(Q[:, :, :1], K[:, :, :1], V[:, :, :1], layer_idx=0)
+
+
+def test_prefill_chunked_validation():
+    c = DropKVCache(keep_ratio=0.3, window_size=8)
+    with pytest.raises(TypeError):
+        prefill_chunked(object(), torch.zeros(1, 100), object())
+    with pytest.raises(ValueError, match="chunk_size.*window_size"):
+        prefill_chunked(object(), torch.zeros(1, 100), c, chunk_size=4)
+    with pytest.raises(ValueError, match="evict_strategy"):
+        prefill_chunked(object(), torch.zeros(1, 100), c, chunk_size=32, evict_strategy="x")
+    with pytest.raises(ValueError, match="window_size"):
+        prefill_chunked(object(), torch.zeros(1, 100), c, chunk_size=32, evict_strategy="budget",
+                        max_kv_tokens=4)
+    with pytest.raises(ValueError, match="sequence-shaped"):
+        prefill_chunked(object(), torch.zeros(1, 100), c, chunk_size=32,
+                        attention_mask=torch.ones(1, 100))
+    c.key_cache.append(torch.zeros(1, 8, 10, 128))
+    c.value_cache.append(torch.zeros(1, 8, 10, 128))
+    with pytest.raises(ValueError, match="fresh.*empty.*cache"):
+        prefill_chunked(object(), torch.zeros(1, 100), c)
+
+
+@pytest.mark.parametrize("strategy", ["last_chunk", "budget"])
+def test_prefill_chunked_cleans_up_after_failure(strategy):
+    calls = {"n": 0}
+
+    def model(ids, past_key_values=None, use_cache=True):
+        calls["n"] += 1
+        if calls["n"] > 1:
+            raise RuntimeError("simulated failure")
+        Q, K, V = _mk(Lq=ids.shape[1], Lk=ids.shape[1])
+        past_key_values._prefill_mode = "accumulate"  # stay on the host: no eviction
+        for layer in range(2):
+            past_key_values.update(Q, K, V, layer_idx=layer)
+
+    c = DropKVCache(keep_ratio=0.3, window_size=8)
+    with pytest.raises(RuntimeError, match="simulated failure"):
+        prefill_chunked(model, torch.zeros(1, 100), c, chunk_size=32, evict_strategy=strategy,
+                        max_kv_tokens=64)
+    assert len(c.key_cache) == 0 and len(c.value_cache) == 0 and c._seen_tokens == 0
+    assert c._prefill_mode == "single_pass"
+    assert c._evict_use_seen_tokens is False and c._budget_max_kv_tokens is None
+
+
+def test_dynamic_cache_helpers():
+    Q, K, V = _mk(Lq=16, Lk=16)
+    c = dropkv_b200.DynamicCache()
+    c.update(None, K, V, 0)
+    c.update(None, K[:, :, :4], V[:, :, :4], 0)
+    assert c.get_seq_length() == 20 and len(c) == 1
+    legacy = c.to_legacy_cache()
+    c2 = dropkv_b200.DynamicCache.from_legacy_cache(legacy)
+    assert torch.equal(c2.key_cache[0], c.key_cache[0])
+    c2.crop(10)
+    assert c2.get_seq_length() == 10
