@@ -28,6 +28,10 @@ SIGNATURES = {
     "dropkv_scores": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_int,
                                _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int, _c_p,
                                _c_p, _c_sz, _c_p]),
+    "dropkv_scorer_for": (_c_int, [_c_int] * 7),
+    "dropkv_set_scorer": (_c_int, [_c_int]),
+    "dropkv_scores_status_offset": (_c_sz, [_c_int] * 7),
+    "dropkv_selftest_tcgen05": (_c_int, [_c_int, _c_p, _c_p, _c_int, _c_p, _c_p, _c_p]),
     "dropkv_select_workspace_size": (_c_sz, [_c_int] * 3),
     "dropkv_select": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_p, _c_p,
                                _c_sz, _c_p]),
@@ -78,6 +82,15 @@ def check(rc: int, what: str = "") -> None:
     if rc != OK:
         msg = load().dropkv_last_error().decode(errors="replace")
         raise DropKVError(rc, f"{what}: {msg}" if what else msg)
+
+
+SCORER_AUTO, SCORER_CUDA_CORES, SCORER_TENSOR_CORES = 0, 1, 2
+NO_STATUS = ctypes.c_size_t(-1).value
+
+
+def set_scorer(mode: int) -> None:
+    """Process-wide scorer choice (0 auto, 1 CUDA cores, 2 tensor cores)."""
+    check(load().dropkv_set_scorer(int(mode)), "dropkv_set_scorer")
 
 
 def launch_count() -> int:

@@ -128,7 +128,23 @@ static int check_ws(void* ws, size_t have, size_t need) {
   return DROPKV_OK;
 }
 
+static std::atomic<int> g_backend{0};  // 0 auto, 1 CUDA-core scorer, 2 tensor-core scorer
+
+static bool use_tc(int dtype, int B, int Hkv, int Lk, int M, int D) {
+  const int be = g_backend.load(std::memory_order_relaxed);
+  if (be == 1) return false;
+  return tc_supported(dtype, M, D, B * Hkv, Lk);
+}
+
+static size_t scores_ws_bytes(int dtype, int B, int Hkv, int Lk, int M, int D) {
+  if (use_tc(dtype, B, Hkv, Lk, M, D)) return tc_workspace_bytes(M, D, B * Hkv, Lk);
+  return plan_scores(B, Hkv, Lk, M, D).bytes;
+}
+
 static int run_scores(const ScoreProblem& p, int dtype, void* ws, cudaStream_t st) {
+  if (use_tc(dtype, p.B, p.Hkv, p.Lk, p.M, p.D)) return launch_scores_tc(p, dtype, ws, st);
+  if (g_backend.load(std::memory_order_relaxed) == 2)
+    return fail(DROPKV_ERR_UNSUPPORTED, "tensor-core scorer forced but it does not cover this problem");
   ScorePlan plan = plan_scores(p.B, p.Hkv, p.Lk, p.M, p.D);
   return launch_scores_simt(p, plan, ws, st, dtype);
 }
@@ -158,7 +174,28 @@ uint64_t dropkv_launch_count(void) { return g_launches.load(std::memory_order_re
 
 size_t dropkv_scores_workspace_size(int B, int Hq, int Hkv, int Lk, int D, int window) {
   if (B < 1 || Hq < 1 || Hkv < 1 || Lk < 1 || D < 1 || window < 1 || Hq % Hkv) return 0;
-  return plan_scores(B, Hkv, Lk, (Hq / Hkv) * window, D).bytes;
+  const int M = (Hq / Hkv) * window;
+  size_t a = scores_ws_bytes(DROPKV_DTYPE_BF16, B, Hkv, Lk, M, D);
+  size_t b = scores_ws_bytes(DROPKV_DTYPE_F32, B, Hkv, Lk, M, D);
+  return a > b ? a : b;
+}
+
+size_t dropkv_scores_status_offset(int dtype, int B, int Hq, int Hkv, int Lk, int D, int window) {
+  if (B < 1 || Hq < 1 || Hkv < 1 || Lk < 1 || D < 1 || window < 1 || Hq % Hkv) return (size_t)-1;
+  const int M = (Hq / Hkv) * window;
+  if (!use_tc(dtype, B, Hkv, Lk, M, D)) return (size_t)-1;
+  return tc_status_offset(M, D, B * Hkv, Lk);
+}
+
+int dropkv_set_scorer(int mode) {
+  if (mode < 0 || mode > 2) return fail(DROPKV_ERR_ARG, "scorer mode must be 0 (auto), 1 (CUDA cores) or 2 (tensor cores)");
+  g_backend.store(mode);
+  return DROPKV_OK;
+}
+
+int dropkv_scorer_for(int dtype, int B, int Hq, int Hkv, int Lk, int D, int window) {
+  if (B < 1 || Hq < 1 || Hkv < 1 || Lk < 1 || D < 1 || window < 1 || Hq % Hkv) return 0;
+  return use_tc(dtype, B, Hkv, Lk, (Hq / Hkv) * window, D) ? 2 : 1;
 }
 
 int dropkv_scores(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
@@ -188,6 +225,9 @@ int dropkv_select(const float* scores, int B, int Hkv, int Lk, int kernel_size, 
   if (!scores || !keep_idx) return fail(DROPKV_ERR_ARG, "scores and keep_idx must be non-NULL");
   if ((rc = check_ws(workspace, workspace_bytes, dropkv_select_workspace_size(B, Hkv, Lk)))) return rc;
   int protect = std::min(protect_window, Lk);
+  if (select_gather_supported(Lk, kernel_size))
+    return launch_select_gather(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, nullptr, nullptr,
+                                4, 1, nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream));
   return launch_select(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, workspace,
                        reinterpret_cast<cudaStream_t>(stream));
 }
@@ -230,6 +270,9 @@ int dropkv_compress(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int
                                 round_p, scores);
   if ((rc = run_scores(p, dtype, workspace, st))) return rc;
   int protect = std::min(protect_window, Lk);
+  if (select_gather_supported(Lk, kernel_size))
+    return launch_select_gather(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, k, v,
+                                elem_bytes_of(dtype), D, k_out, v_out, st);
   if ((rc = launch_select(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, sel_ws, st))) return rc;
   return launch_gather(k, v, elem_bytes_of(dtype), B * Hkv, Lk, D, keep_idx, keep_len, k_out, v_out, st);
 }

@@ -89,6 +89,10 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // Launchers implemented per translation unit.
 int launch_scores_simt(const ScoreProblem& p, const ScorePlan& plan, void* ws, cudaStream_t st,
                        int dtype);
+bool tc_supported(int dtype, int M, int D, int BH, int Lk);
+size_t tc_workspace_bytes(int M, int D, int BH, int Lk);
+size_t tc_status_offset(int M, int D, int BH, int Lk);
+int launch_scores_tc(const ScoreProblem& p, int dtype, void* ws, cudaStream_t st);
 
 struct SelectPlan {
   size_t off_keys;   // uint32 [BH, Lk]
@@ -97,6 +101,11 @@ struct SelectPlan {
 SelectPlan plan_select(int BH, int Lk);
 int launch_select(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
                   int64_t* keep_idx, void* ws, cudaStream_t st);
+bool select_gather_supported(int Lk, int kernel_size);
+// k == nullptr: selection only (keep_idx), no gather
+int launch_select_gather(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
+                         int64_t* keep_idx, const void* k, const void* v, int elem_bytes, int D, void* ko,
+                         void* vo, cudaStream_t st);
 int launch_gather(const void* k, const void* v, int elem_bytes, int BH, int Lk, int D,
                   const int64_t* keep_idx, int keep_len, void* k_out, void* v_out,
                   cudaStream_t st);

@@ -1,0 +1,938 @@
+// Fused tensor-core DropKV scorer for sm_100a (bf16 / fp16 inputs, D in {64, 128},
+// M = g*W <= 64 query rows per KV head).
+//
+// One persistent cooperative launch, one CTA per SM.  CTAs form `groups` groups
+// of `gs` CTAs; group g scores heads g, g + groups, ... one round at a time, and
+// CTA `rank` of a group owns a contiguous range of <= tmax 128-key tiles of the
+// round's head.  Warp roles inside a CTA (coupled only through mbarriers):
+//   warp 8     TMA producer: K, V, V tiles of every round into an NS-slot ring;
+//   warp 9     MMA issuer (one thread) and TMEM owner;
+//   warps 0-7  epilogue: warp w reads TMEM lanes 32*(w%4).. (32 keys of a tile)
+//              and query columns [(w/4)*N/2, (w/4+1)*N/2).
+// Per head and CTA:
+//
+//   pass 1  K tiles stream in by TMA (L2 evict-first); tcgen05 computes the logit
+//           tile S = K Q^T (keys on the MMA M axis, the M query rows on N) into
+//           TMEM, where it stays for pass 2.  The CTA-local softmax max m and sum s
+//           per query row follow from the TMEM tiles; p = exp(l - m) is split into
+//           bf16/fp16 hi + lo halves in shared memory and V tiles (TMA, L2
+//           evict-last so pass 2 finds them in L2) give y^T += V^T p_hi^T + V^T p_lo^T
+//           (fp32 accumulation in TMEM: y keeps ~16 mantissa bits of p).
+//           The partial (m, s, y) goes to global memory.
+//   merge   group barrier; each CTA merges a 1/gs slice of the head's M x D
+//           elements of y with the max-rescale rule (dropkv_triton.py:441-452),
+//           plus lse; group barrier.
+//   pass 2  y is split hi + lo into shared memory; V tiles come back by TMA
+//           (L2 hits); tcgen05 gives <v_j, y_m> = V (y_hi + y_lo)^T in TMEM; the
+//           epilogue (one thread per key, all M rows in registers) forms
+//           p = exp(l - lse) clamped to [0,1] (rounded to the input dtype when
+//           requested), w = (p / (1 - p + eps))^2 and
+//           score_j = (sum w ||v_j||^2 - 2 sum w <v_j,y_m> + sum w ||y_m||^2) / g,
+//           the reference's termA - termB + termC (dropkv_triton.py:94-108).
+//
+// Group barriers are bounded spins on global counters (zeroed by the host before
+// the launch); every wait in the kernel gives up after a timeout, records a
+// device status and lets the CTA run to its end without further waits, so a
+// fault in this logic ends the kernel instead of hanging the GPU.
+#include <cmath>
+#include <cstring>
+#include <type_traits>
+
+#include "tc_common.cuh"
+
+namespace dropkv {
+
+// ---------------------------------------------------------------------------
+// Tensor map (host)
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int make_kv_tensor_map(CUtensorMap* map, const void* base, int BH, int L, int D, bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(DROPKV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  if (reinterpret_cast<uintptr_t>(base) % 16) return fail(DROPKV_ERR_ARG, "K/V must be 16-byte aligned");
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)L, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)L * D * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DROPKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DROPKV_OK;
+}
+
+
+namespace {
+
+constexpr int TK = 128;                      // keys per tile = MMA M
+constexpr int NEPI = 256;                    // epilogue threads (warps 0-7)
+constexpr int NTH = NEPI + 64;               // + TMA producer warp (8) + MMA warp (9)
+constexpr int WARP_TMA = 8, WARP_MMA = 9;
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
+constexpr int kMaxGs = 256;                  // CTAs per head group (at most)
+constexpr int kWts = 1024;                   // merge-weight buffer (floats)
+constexpr int kMaxTiles = 30;                // TMEM logit tiles per CTA and head (N = 16)
+
+struct TcArgs {
+  ScoreProblem p;
+  int BH;
+  int gs, groups, rounds, tiles, tmax;
+  float c;       // log2(e) / sqrt(D): logits in the base-2 domain
+  float pscale;  // scale of p before the hi/lo split (2^15 for fp16, 1 for bf16)
+  int* ctr;      // [2 * BH] group-barrier counters (zero at launch)
+  float* part_m; // [BH][gs][M]  (base-2 max)
+  float* part_s; // [BH][gs][M]
+  float* part_y; // [BH][gs][M][D]
+  float* y_g;    // [BH][M][D]
+  float* lse_g;  // [BH][M]      (base-2)
+  int* status;   // device status word (0 = ok)
+  unsigned long long* trace;  // per CTA and round: globaltimer at phase ends
+};
+
+// Phase timestamps recorded by epilogue thread 0 of every CTA (ns, globaltimer):
+// trace[3 + (cta * rounds + round) * kTraceEv + ev]; trace[0..2] = {ctas, rounds, kTraceEv}.
+enum { TR_START, TR_LOGITS, TR_MAX, TR_PV, TR_BAR_A, TR_MERGE, TR_BAR_B, TR_YSTAGE, TR_PASS2, kTraceEv };
+
+template <int D, int NPAD, int NS>
+struct Lay {
+  static constexpr int TILE = TK * D * 2;         // one K or V tile
+  static constexpr int RB = NPAD * 128;           // one SW128 region of NPAD rows
+  static constexpr int TMAX = (512 - 2 * NPAD) / NPAD;
+  static constexpr int RING = 0;
+  static constexpr int QS = RING + NS * TILE;     // D/64 regions
+  static constexpr int PS = QS + (D / 64) * RB;   // [buf 2][hi/lo 2][key half 2] regions
+  static constexpr int YS = PS + 8 * RB;          // [hi/lo 2][D/64] regions
+  static constexpr int FL = YS + 2 * (D / 64) * RB;
+  static constexpr int MLOC = FL;                 // floats [NPAD]
+  static constexpr int LSE = MLOC + 4 * NPAD;
+  static constexpr int YN = LSE + 4 * NPAD;
+  static constexpr int BND = YN + 4 * NPAD;       // int [NPAD] causal bound per row
+  static constexpr int RED = BND + 4 * NPAD;      // [8 warps][NPAD]
+  static constexpr int XCH = RED + 32 * NPAD;     // [2 buf][3][TK] pass-2 half exchange
+  static constexpr int WTS = XCH + 4 * 6 * TK;    // [kWts]
+  static constexpr int VN = WTS + 4 * kWts;       // [2 halves][TMAX][TK]
+  static constexpr int BAR = VN + 8 * TMAX * TK;  // mbarriers
+  static constexpr int NBAR = 2 * NS + kMaxTiles + 12;
+  static constexpr int MISC = BAR + 8 * NBAR;     // tmem slot, flags
+  static constexpr int BYTES = MISC + 64;
+  static constexpr int ALLOC = BYTES + 1024;      // + alignment slack
+};
+
+// mbarrier indices after full[NS], free[NS] and s_done[kMaxTiles]
+enum {
+  B_QREADY = 0, B_PREADY0, B_PREADY1, B_PFREE0, B_PFREE1, B_YDONE, B_YREADY,
+  B_S2READY0, B_S2READY1, B_S2FREE0, B_S2FREE1, B_FIN, kAuxBars
+};
+
+template <typename T>
+__device__ __forceinline__ uint16_t to_bits(float x);
+template <>
+__device__ __forceinline__ uint16_t to_bits<__nv_bfloat16>(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+template <>
+__device__ __forceinline__ uint16_t to_bits<__half>(float x) {
+  return __half_as_ushort(__float2half_rn(x));
+}
+template <typename T>
+__device__ __forceinline__ float from_bits(uint16_t b);
+template <>
+__device__ __forceinline__ float from_bits<__nv_bfloat16>(uint16_t b) {
+  return __bfloat162float(__ushort_as_bfloat16(b));
+}
+template <>
+__device__ __forceinline__ float from_bits<__half>(uint16_t b) {
+  return __half2float(__ushort_as_half(b));
+}
+
+template <int ROUND>
+__device__ __forceinline__ float round_p_t(float p) {
+  if (ROUND == DROPKV_ROUND_BF16) return __bfloat162float(__float2bfloat16_rn(p));
+  if (ROUND == DROPKV_ROUND_F16) return __half2float(__float2half_rn(p));
+  return p;
+}
+
+// C columns per lane (C a power of two <= 32): lane l returns column (l % C)
+// reduced over all 32 lanes.  log2(C) transpose steps, then the remaining lanes.
+template <int C, bool MAX>
+__device__ __forceinline__ float col_reduce(float (&v)[C], int lane) {
+#pragma unroll
+  for (int s = C / 2; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int i = 0; i < s; ++i) {
+      const float send = upper ? v[i] : v[i + s];
+      const float keep = upper ? v[i + s] : v[i];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+      v[i] = MAX ? fmaxf(keep, recv) : keep + recv;
+    }
+  }
+  float r = v[0];
+#pragma unroll
+  for (int s = C; s < 32; s <<= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, r, s);
+    r = MAX ? fmaxf(r, o) : r + o;
+  }
+  return r;
+}
+
+// TMEM -> registers, C fp32 columns of this thread's lane (C in {8, 16, 32}).
+template <int C>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v);
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float* v) { tc::tmem_ld32(taddr, v); }
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float* v) { tc::tmem_ld16(taddr, v); }
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, float* v) { tc::tmem_ld8(taddr, v); }
+
+__device__ __forceinline__ void epi_sync() {  // named barrier of the 256 epilogue threads
+  asm volatile("bar.sync 1, %0;" ::"r"(NEPI) : "memory");
+}
+__device__ __forceinline__ void pair_sync(int q) {  // the two warps of TMEM quadrant q
+  asm volatile("bar.sync %0, 64;" ::"r"(2 + q) : "memory");
+}
+
+template <typename T, int D, int NPAD, int NS, int ROUND>
+__global__ void __launch_bounds__(NTH, 1)
+    fused_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                        TcArgs a) {
+  using L = Lay<D, NPAD, NS>;
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int NREG = D / 64;            // 64-wide slabs of a K/V/Q/Y row
+  constexpr int TMAX = L::TMAX;
+  constexpr int S2COL = TMAX * NPAD;      // y^T accumulator / S2 buffer 0; buffer 1 follows
+  constexpr int HC = NPAD / 2;            // query columns per epilogue warp
+  static_assert(TMAX <= kMaxTiles, "s_done barriers");
+  extern __shared__ uint8_t raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::BAR);
+  uint64_t* freeb = full + NS;
+  uint64_t* sdone = freeb + NS;
+  uint64_t* bx = sdone + kMaxTiles;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + L::MISC);
+  int* abort_flag = reinterpret_cast<int*>(sm + L::MISC + 8);
+  float* mloc = reinterpret_cast<float*>(sm + L::MLOC);
+  float* lse_s = reinterpret_cast<float*>(sm + L::LSE);
+  float* yn_s = reinterpret_cast<float*>(sm + L::YN);
+  int* bnd_s = reinterpret_cast<int*>(sm + L::BND);
+  float* red = reinterpret_cast<float*>(sm + L::RED);
+  float* xch = reinterpret_cast<float*>(sm + L::XCH);
+  float* wts = reinterpret_cast<float*>(sm + L::WTS);
+  float* vn_s = reinterpret_cast<float*>(sm + L::VN);
+
+  const ScoreProblem& p = a.p;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grp = blockIdx.x / a.gs, rank = blockIdx.x % a.gs;
+  const int M = p.M, W = p.W, Lk = p.Lk;
+  const int t0 = (int)(((long long)rank * a.tiles) / a.gs);
+  const int nt = (int)(((long long)(rank + 1) * a.tiles) / a.gs) - t0;
+  const int my_rounds = (grp < a.BH) ? min(a.rounds, (a.BH - grp + a.groups - 1) / a.groups) : 0;
+
+  if (tid == 0) {
+    for (int i = 0; i < L::NBAR; ++i) tc::mbar_init(&full[i], 1);
+    // multi-arrival barriers: one arrival per epilogue warp
+    tc::mbar_init(&bx[B_PREADY0], 8);
+    tc::mbar_init(&bx[B_PREADY1], 8);
+    tc::mbar_init(&bx[B_S2FREE0], 8);
+    tc::mbar_init(&bx[B_S2FREE1], 8);
+    tc::fence_mbar_init();
+    *abort_flag = 0;
+    if (blockIdx.x == 0) {
+      a.trace[0] = gridDim.x;
+      a.trace[1] = a.rounds;
+      a.trace[2] = kTraceEv;
+    }
+  }
+  if (warp == WARP_MMA) {
+    tc::tmem_alloc(tslot, 512);
+    tc::tmem_relinquish();
+  }
+  if (tid < NPAD) {
+    bnd_s[tid] = (tid < M) ? (Lk - W + tid % W) : -1;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  volatile int* vabort = abort_flag;
+  auto fail_wait = [&](int code) {
+    *vabort = 1;
+    atomicOr(a.status, code);
+  };
+  // bounded wait that also gives up as soon as another role aborted
+  auto wait_bar = [&](uint64_t* b, uint32_t parity, int code) -> bool {
+    if (*vabort) return false;
+    if (tc::mbar_try_wait(b, parity)) return true;
+    const uint64_t t_start = tc::globaltimer_ns();
+    while (!tc::mbar_try_wait(b, parity)) {
+      if (*vabort) return false;
+      if (tc::globaltimer_ns() - t_start > kWaitNs) {
+        fail_wait(code);
+        return false;
+      }
+    }
+    return true;
+  };
+
+  if (warp == WARP_TMA) {
+    // ======================= TMA producer =======================================
+    // Load k: round k / (3 nt), stage (k / nt) % 3 (0: K pass 1, 1: V pass 1,
+    // 2: V pass 2), tile k % nt.  V pass-1 loads keep their lines in L2 for pass 2.
+    if (lane == 0) {
+      const uint64_t pol_first = tc::policy_evict_first();
+      const uint64_t pol_last = tc::policy_evict_last();
+      tc::tma_prefetch_desc(&kmap);
+      tc::tma_prefetch_desc(&vmap);
+      const uint32_t total = (uint32_t)my_rounds * 3u * (uint32_t)nt;
+      for (uint32_t k = 0; k < total; ++k) {
+        const uint32_t slot = k % NS;
+        if (k >= NS && !wait_bar(&freeb[slot], ((k / NS) - 1) & 1, 2)) break;
+        const int r = (int)(k / (3u * nt));
+        const int stage = (int)((k / nt) % 3u);
+        const int tile = (int)(k % nt);
+        const int bh = r * a.groups + grp;
+        tc::mbar_arrive_expect_tx(&full[slot], L::TILE);
+        for (int rr = 0; rr < NREG; ++rr)
+          tc::tma_load_3d(sm + L::RING + slot * L::TILE + rr * 16384, stage == 0 ? &kmap : &vmap, &full[slot],
+                          64 * rr, (t0 + tile) * TK, bh, stage == 1 ? pol_last : pol_first);
+      }
+    }
+  } else if (warp == WARP_MMA) {
+    // ======================= MMA issuer ========================================
+    if (lane == 0) {
+      const uint32_t ring0 = tc::smem_addr(sm + L::RING);
+      const uint32_t qs0 = tc::smem_addr(sm + L::QS);
+      const uint32_t ps0 = tc::smem_addr(sm + L::PS);
+      const uint32_t ys0 = tc::smem_addr(sm + L::YS);
+      constexpr uint32_t ID_QK = tc::idesc_f16(BF16, 128, NPAD, false, false);
+      constexpr uint32_t ID_PV = tc::idesc_f16(BF16, 128, NPAD, true, false);
+      constexpr uint32_t LBO_PV = (NREG == 2) ? 16384u : 0u;
+      uint32_t k = 0;  // ring position
+      uint32_t c_pready[2] = {0, 0}, c_s2free[2] = {0, 0};
+      for (int rd = 0; rd < my_rounds && !*vabort; ++rd) {
+        if (!wait_bar(&bx[B_QREADY], rd & 1, 20)) break;
+        tc::tc_fence_after();
+        // pass 1a: S_i = K_i Q^T
+        for (int i = 0; i < nt; ++i, ++k) {
+          const uint32_t slot = k % NS;
+          if (!wait_bar(&full[slot], (k / NS) & 1, 21)) break;
+          tc::tc_fence_after();
+          const uint32_t a0 = ring0 + slot * L::TILE;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t ad = tc::smem_desc(a0 + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024);
+            const uint64_t bd = tc::smem_desc(qs0 + (kk / 4) * L::RB + (kk % 4) * 32, 16, 1024);
+            tc::mma_f16(tmem + i * NPAD, ad, bd, ID_QK, kk > 0);
+          }
+          tc::mma_commit(&freeb[slot]);
+          tc::mma_commit(&sdone[i]);
+        }
+        // pass 1c: y^T += V_i^T (p_hi + p_lo)^T
+        for (int i = 0; i < nt; ++i, ++k) {
+          const uint32_t slot = k % NS;
+          const int buf = i & 1;
+          if (!wait_bar(&full[slot], (k / NS) & 1, 22)) break;
+          if (!wait_bar(&bx[B_PREADY0 + buf], c_pready[buf] & 1, 23)) break;
+          ++c_pready[buf];
+          tc::tc_fence_after();
+          const uint32_t a0 = ring0 + slot * L::TILE;
+          const uint32_t pb = ps0 + buf * 4 * L::RB;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t ad = tc::smem_desc(a0 + kk * 2048, LBO_PV, 1024);
+              const uint64_t bd = tc::smem_desc(pb + half * 2 * L::RB + (kk / 4) * L::RB + (kk % 4) * 32, 16, 1024);
+              tc::mma_f16(tmem + S2COL, ad, bd, ID_PV, (i > 0 || half > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc::mma_commit(&freeb[slot]);
+          tc::mma_commit(&bx[B_PFREE0 + buf]);
+        }
+        tc::mma_commit(&bx[B_YDONE]);
+        // pass 2: S2_i = V_i (y_hi + y_lo)^T
+        if (!wait_bar(&bx[B_YREADY], rd & 1, 24)) break;
+        tc::tc_fence_after();
+        for (int i = 0; i < nt; ++i, ++k) {
+          const uint32_t slot = k % NS;
+          const int buf = i & 1;
+          if (!wait_bar(&full[slot], (k / NS) & 1, 25)) break;
+          if (i >= 2) {
+            if (!wait_bar(&bx[B_S2FREE0 + buf], c_s2free[buf] & 1, 26)) break;
+            ++c_s2free[buf];
+          }
+          tc::tc_fence_after();
+          const uint32_t a0 = ring0 + slot * L::TILE;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t ad = tc::smem_desc(a0 + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024);
+              const uint64_t bd = tc::smem_desc(ys0 + half * NREG * L::RB + (kk / 4) * L::RB + (kk % 4) * 32, 16, 1024);
+              tc::mma_f16(tmem + S2COL + buf * NPAD, ad, bd, ID_QK, (half > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc::mma_commit(&freeb[slot]);
+          tc::mma_commit(&bx[B_S2READY0 + buf]);
+        }
+        // the last (up to two) S2 buffers are released after this round's epilogue
+        for (int i = (nt >= 2 ? nt - 2 : 0); i < nt; ++i) {
+          const int buf = i & 1;
+          if (!wait_bar(&bx[B_S2FREE0 + buf], c_s2free[buf] & 1, 27)) break;
+          ++c_s2free[buf];
+        }
+      }
+      tc::mma_commit(&bx[B_FIN]);
+      if (!tc::mbar_wait(&bx[B_FIN], 0, kWaitNs)) atomicOr(a.status, 28);
+    }
+  } else {
+    // ======================= epilogue: warps 0-7 ==============================
+    const int q = warp & 3;              // TMEM lane quadrant: keys 32q .. 32q+31 of a tile
+    const int ch = warp >> 2;            // query-column half
+    const int et = tid;                  // 0 .. 255
+    const int jkey = q * 32 + lane;      // key within a tile
+    const uint32_t lrow = (uint32_t)(q * 32) << 16;
+    const int cbase = ch * HC;
+    uint32_t c_pfree[2] = {0, 0}, c_s2r[2] = {0, 0};
+    const bool stamper = (et == 0);
+    auto stamp = [&](int rd, int ev) {
+      if (stamper) a.trace[3 + ((size_t)blockIdx.x * a.rounds + rd) * kTraceEv + ev] = tc::globaltimer_ns();
+    };
+    // which of my columns are real query rows
+    bool colok[HC];
+#pragma unroll
+    for (int j = 0; j < HC; ++j) colok[j] = (cbase + j) < M;
+
+    for (int rd = 0; rd < my_rounds; ++rd) {
+      const int h = rd * a.groups + grp;
+      const int b = h / p.Hkv, hkv = h % p.Hkv;
+      stamp(rd, TR_START);
+
+      // ---- Q window -> SW128 K-major operand ----------------------------------
+      {
+        const T* qp = reinterpret_cast<const T*>(p.q);
+#pragma unroll 4
+        for (int i = et; i < NPAD * D; i += NEPI) {
+          const int m = i / D, d = i % D;
+          uint16_t v = 0;
+          if (m < M) {
+            const int qh = hkv * p.g + m / W;
+            const int qpos = p.Lq - W + m % W;
+            const T x = qp[(int64_t)b * p.q_sb + (int64_t)qh * p.q_sh + (int64_t)qpos * p.q_ss + (int64_t)d * p.q_sd];
+            v = *reinterpret_cast<const uint16_t*>(&x);
+          }
+          *reinterpret_cast<uint16_t*>(sm + L::QS + (d / 64) * L::RB + tc::sw128_offset(m, d % 64)) = v;
+        }
+        tc::fence_proxy_async_smem();
+        tc::tc_fence_before();
+        epi_sync();
+        if (et == 0) tc::mbar_arrive(&bx[B_QREADY]);
+      }
+
+      // ---- pass 1b: local max per query row, as logit tiles complete ----------
+      float mx[HC];
+#pragma unroll
+      for (int j = 0; j < HC; ++j) mx[j] = -INFINITY;
+      for (int i = 0; i < nt; ++i) {
+        wait_bar(&sdone[i], rd & 1, 30);
+        tc::tc_fence_after();
+        float s[HC];
+        tmem_ld<HC>(tmem + lrow + i * NPAD + cbase, s);
+        const int key = (t0 + i) * TK + jkey;
+        const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
+#pragma unroll
+        for (int j = 0; j < HC; ++j) {
+          const bool ok = edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j];
+          mx[j] = fmaxf(mx[j], ok ? s[j] * a.c : -INFINITY);
+        }
+      }
+      stamp(rd, TR_LOGITS);
+      {
+        const float col = col_reduce<HC, true>(mx, lane);
+        if (lane < HC) red[q * NPAD + cbase + lane] = col;
+      }
+      epi_sync();
+      if (et < NPAD) {
+        float m4 = red[et];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) m4 = fmaxf(m4, red[w * NPAD + et]);
+        mloc[et] = m4;
+      }
+      epi_sync();
+      stamp(rd, TR_MAX);
+
+      // ---- pass 1c: p = exp2(l - m) -> hi/lo P tiles; ||v||^2 -------------------
+      float ssum[HC];
+#pragma unroll
+      for (int j = 0; j < HC; ++j) ssum[j] = 0.f;
+      float ml[HC];
+#pragma unroll
+      for (int j = 0; j < HC; ++j) ml[j] = mloc[cbase + j];
+      for (int i = 0; i < nt; ++i) {
+        const int buf = i & 1;
+        const uint32_t kpos = (uint32_t)rd * 3u * nt + nt + i;  // ring position of V tile i
+        const uint32_t slot = kpos % NS;
+        if (i >= 2) {
+          wait_bar(&bx[B_PFREE0 + buf], c_pfree[buf] & 1, 31);
+          ++c_pfree[buf];
+        }
+        float s[HC];
+        tc::tc_fence_after();
+        tmem_ld<HC>(tmem + lrow + i * NPAD + cbase, s);
+        const int key = (t0 + i) * TK + jkey;
+        const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
+        uint8_t* pb = sm + L::PS + buf * 4 * L::RB + (jkey >> 6) * L::RB;
+#pragma unroll
+        for (int j = 0; j < HC; ++j) {
+          const int m = cbase + j;
+          const bool ok = (edge ? (key <= bnd_s[m] && key < Lk) : colok[j]) && ml[j] != -INFINITY;
+          const float pr = ok ? exp2f(fmaf(s[j], a.c, -ml[j])) : 0.f;
+          ssum[j] += pr;
+          const float ps = pr * a.pscale;
+          const uint16_t hi = to_bits<T>(ps);
+          const uint16_t lo = to_bits<T>(ps - from_bits<T>(hi));
+          const uint32_t off = tc::sw128_offset(m, jkey & 63);
+          *reinterpret_cast<uint16_t*>(pb + off) = hi;
+          *reinterpret_cast<uint16_t*>(pb + 2 * L::RB + off) = lo;
+        }
+        // V tile i: read it for ||v||^2 before it may be released (the P.V MMA
+        // runs only after every warp's p_ready arrival below)
+        wait_bar(&full[slot], (kpos / NS) & 1, 32);
+        // ||v_j||^2, this warp's 64-wide slab of the row (D = 64: half 1 has none)
+        {
+          float acc = 0.f;
+          if (ch < NREG) {
+            const uint8_t* vt = sm + L::RING + slot * L::TILE + ch * 16384 + jkey * 128;
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8) {
+              const uint4 r4 = *reinterpret_cast<const uint4*>(vt + ((c8 ^ (jkey & 7)) << 4));
+              const uint32_t w4[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+              for (int k2 = 0; k2 < 4; ++k2) {
+                const float x0 = from_bits<T>((uint16_t)(w4[k2] & 0xffffu));
+                const float x1 = from_bits<T>((uint16_t)(w4[k2] >> 16));
+                acc = fmaf(x0, x0, acc);
+                acc = fmaf(x1, x1, acc);
+              }
+            }
+          }
+          vn_s[(ch * TMAX + i) * TK + jkey] = acc;
+        }
+        tc::fence_proxy_async_smem();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bx[B_PREADY0 + buf]);
+      }
+      // y^T complete
+      if (nt > 0) wait_bar(&bx[B_YDONE], rd & 1, 33);
+      // the P buffers of the last one or two tiles were released by that too
+      for (int i = (nt >= 2 ? nt - 2 : 0); i < nt; ++i) {
+        const int buf = i & 1;
+        wait_bar(&bx[B_PFREE0 + buf], c_pfree[buf] & 1, 34);
+        ++c_pfree[buf];
+      }
+      tc::tc_fence_after();
+      stamp(rd, TR_PV);
+
+      // ---- partial (m, s, y) of this CTA -----------------------------------------
+      {
+        const float col = col_reduce<HC, false>(ssum, lane);
+        if (lane < HC) red[q * NPAD + cbase + lane] = col;
+      }
+      epi_sync();
+      const size_t prow = ((size_t)h * a.gs + rank) * M;
+      if (et < M) {
+        const float s4 = red[et] + red[NPAD + et] + red[2 * NPAD + et] + red[3 * NPAD + et];
+        __stcg(a.part_m + prow + et, mloc[et]);
+        __stcg(a.part_s + prow + et, s4);
+      }
+      {
+        const float inv = 1.0f / a.pscale;
+        const int d = q * 32 + lane;  // TMEM lane of the y^T accumulator = d
+        if (d < D) {
+          float v[HC];
+          if (nt > 0) tmem_ld<HC>(tmem + lrow + S2COL + cbase, v);
+#pragma unroll
+          for (int j = 0; j < HC; ++j)
+            if (colok[j]) __stcg(a.part_y + (prow + cbase + j) * D + d, nt > 0 ? v[j] * inv : 0.f);
+        }
+      }
+      tc::tc_fence_before();
+
+      // ---- group barrier A, distributed merge, group barrier B --------------------
+      auto group_barrier = [&](int* ctr) {
+        epi_sync();
+        if (et == 0 && !*vabort) {
+          __threadfence();
+          atomicAdd(ctr, 1);
+          const uint64_t t_start = tc::globaltimer_ns();
+          while (true) {
+            int v;
+            asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+            if (v >= a.gs) break;
+            if (*vabort) break;
+            if (tc::globaltimer_ns() - t_start > kWaitNs) { fail_wait(35); break; }
+          }
+          __threadfence();
+        }
+        epi_sync();
+      };
+      group_barrier(a.ctr + 2 * h);
+      stamp(rd, TR_BAR_A);
+      {
+        const int E = M * D;
+        const int e0 = (int)(((long long)rank * E) / a.gs), e1 = (int)(((long long)(rank + 1) * E) / a.gs);
+        const int ne = e1 - e0;
+        const size_t hb = (size_t)h * a.gs;
+        float* acc = reinterpret_cast<float*>(sm + L::PS);  // P buffers are idle here
+        if (ne > 0) {
+          const int m_lo = e0 / D, nrow = (e1 - 1) / D - m_lo + 1;
+          const int npairs = a.gs * ne;
+          const int nst = nrow * a.gs;
+          float* sts = acc + npairs;  // part_s of the slice rows
+          // one round trip: maxima, sums and every (partial, element) value of the slice
+          for (int k0 = 0; k0 < npairs + 2 * nst; k0 += 8 * NEPI) {
+            float val[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int k = k0 + u * NEPI + et;
+              val[u] = 0.f;
+              if (k < npairs) {
+                const int c = k / ne, e = k % ne;
+                const int eg = e0 + e, m = eg / D, d = eg % D;
+                val[u] = __ldcg(a.part_y + ((hb + c) * M + m) * D + d);
+              } else if (k < npairs + nst) {
+                const int kk = k - npairs, r = kk / a.gs, c = kk % a.gs;
+                val[u] = __ldcg(a.part_m + (hb + c) * M + m_lo + r);
+              } else if (k < npairs + 2 * nst) {
+                const int kk = k - npairs - nst, r = kk / a.gs, c = kk % a.gs;
+                val[u] = __ldcg(a.part_s + (hb + c) * M + m_lo + r);
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int k = k0 + u * NEPI + et;
+              if (k < npairs) acc[k] = val[u];
+              else if (k < npairs + nst) wts[k - npairs] = val[u];
+              else if (k < npairs + 2 * nst) sts[k - npairs - nst] = val[u];
+            }
+          }
+          epi_sync();
+          for (int r = warp; r < nrow; r += NEPI / 32) {
+            float mxr = -INFINITY;
+            for (int c = lane; c < a.gs; c += 32) mxr = fmaxf(mxr, wts[r * a.gs + c]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mxr = fmaxf(mxr, __shfl_xor_sync(0xffffffffu, mxr, o));
+            float tot = 0.f;
+            for (int c = lane; c < a.gs; c += 32) {
+              const float pm = wts[r * a.gs + c];
+              const float w = (pm == -INFINITY) ? 0.f : exp2f(pm - mxr);
+              wts[r * a.gs + c] = w;
+              tot = fmaf(w, sts[r * a.gs + c], tot);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+            if (lane == 0) {
+              red[r] = tot;
+              red[NPAD + r] = mxr;
+            }
+          }
+          epi_sync();
+          // fixed-order weighted sums (deterministic); SPL threads per element
+          const int spl = max(1, min(8, 512 / ne));
+          for (int idx = et; idx < ne * spl; idx += NEPI) {
+            const int e = idx / spl, sp = idx % spl;
+            const int eg = e0 + e, m = eg / D;
+            const float* wr = wts + (m - m_lo) * a.gs;
+            float sacc = 0.f;
+            for (int c = sp; c < a.gs; c += spl) sacc = fmaf(wr[c], acc[c * ne + e], sacc);
+            if (spl == 1) __stcg(a.y_g + (size_t)h * E + eg, sacc / red[m - m_lo]);
+            else xch[idx] = sacc;
+          }
+          if (spl > 1) {
+            epi_sync();
+            for (int e = et; e < ne; e += NEPI) {
+              float sacc = 0.f;
+              for (int sp = 0; sp < spl; ++sp) sacc += xch[e * spl + sp];
+              const int eg = e0 + e, m = eg / D;
+              __stcg(a.y_g + (size_t)h * E + eg, sacc / red[m - m_lo]);
+            }
+          }
+          if (et < nrow && e0 <= (m_lo + et) * D)
+            __stcg(a.lse_g + (size_t)h * M + m_lo + et, red[NPAD + et] + log2f(red[et]));
+        }
+      }
+      stamp(rd, TR_MERGE);
+      group_barrier(a.ctr + 2 * h + 1);
+      stamp(rd, TR_BAR_B);
+
+      // ---- y (hi/lo) -> shared memory; lse, ||y||^2 --------------------------------
+      {
+        constexpr int TPRY = (NEPI / NPAD < D / 8) ? NEPI / NPAD : D / 8;  // threads per row
+        constexpr int DPT = D / TPRY;
+        const int m = et / TPRY, dbase = (et % TPRY) * DPT;
+        float n2 = 0.f;
+        if (m < NPAD) {
+#pragma unroll
+          for (int d8 = 0; d8 < DPT; d8 += 8) {
+            const int d = dbase + d8;
+            float y[8];
+            if (m < M) {
+              const float4 u0 = __ldcg(reinterpret_cast<const float4*>(a.y_g + ((size_t)h * M + m) * D + d));
+              const float4 u1 = __ldcg(reinterpret_cast<const float4*>(a.y_g + ((size_t)h * M + m) * D + d + 4));
+              y[0] = u0.x; y[1] = u0.y; y[2] = u0.z; y[3] = u0.w;
+              y[4] = u1.x; y[5] = u1.y; y[6] = u1.z; y[7] = u1.w;
+            } else {
+#pragma unroll
+              for (int k2 = 0; k2 < 8; ++k2) y[k2] = 0.f;
+            }
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int k2 = 0; k2 < 8; k2 += 2) {
+              n2 = fmaf(y[k2], y[k2], n2);
+              n2 = fmaf(y[k2 + 1], y[k2 + 1], n2);
+              const uint16_t h0 = to_bits<T>(y[k2]), h1 = to_bits<T>(y[k2 + 1]);
+              const uint16_t l0 = to_bits<T>(y[k2] - from_bits<T>(h0));
+              const uint16_t l1 = to_bits<T>(y[k2 + 1] - from_bits<T>(h1));
+              hw[k2 / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+              lw[k2 / 2] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+            }
+            const uint32_t off = (d / 64) * L::RB + m * 128 + ((((d % 64) >> 3) ^ (m & 7)) << 4);
+            *reinterpret_cast<uint4*>(sm + L::YS + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4*>(sm + L::YS + NREG * L::RB + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+          }
+        }
+#pragma unroll
+        for (int o = 1; o < TPRY; o <<= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, o);
+        if (m < NPAD && et % TPRY == 0) {
+          yn_s[m] = n2;
+          lse_s[m] = (m < M) ? __ldcg(a.lse_g + (size_t)h * M + m) : 0.f;
+        }
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      epi_sync();
+      if (et == 0) tc::mbar_arrive(&bx[B_YREADY]);
+      stamp(rd, TR_YSTAGE);
+
+      // ---- pass 2: score epilogue over S (TMEM, pass 1) and S2 = <v, y> ------------
+      float lsel[HC], ynl[HC];
+#pragma unroll
+      for (int j = 0; j < HC; ++j) {
+        lsel[j] = lse_s[cbase + j];
+        ynl[j] = yn_s[cbase + j];
+      }
+      for (int i = 0; i < nt; ++i) {
+        const int buf = i & 1;
+        wait_bar(&bx[B_S2READY0 + buf], c_s2r[buf] & 1, 36);
+        ++c_s2r[buf];
+        tc::tc_fence_after();
+        float s[HC], s2[HC];
+        tmem_ld<HC>(tmem + lrow + i * NPAD + cbase, s);
+        tmem_ld<HC>(tmem + lrow + S2COL + buf * NPAD + cbase, s2);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bx[B_S2FREE0 + buf]);
+        const int key = (t0 + i) * TK + jkey;
+        const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
+        float sw = 0.f, sb = 0.f, sc = 0.f;
+#pragma unroll
+        for (int j = 0; j < HC; ++j) {
+          const bool ok = edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j];
+          float pr = exp2f(fmaf(s[j], a.c, -lsel[j]));
+          pr = fminf(pr, 1.f);
+          pr = round_p_t<ROUND>(pr);
+          const float ratio = __fdividef(pr, 1.f - pr + p.eps);
+          const float w = ok ? ratio * ratio : 0.f;
+          sw += w;
+          sb = fmaf(w, s2[j], sb);
+          sc = fmaf(w, ynl[j], sc);
+        }
+        float* xb = xch + buf * 3 * TK;
+        if (ch == 1) {
+          xb[jkey] = sw;
+          xb[TK + jkey] = sb;
+          xb[2 * TK + jkey] = sc;
+        }
+        pair_sync(q);
+        if (ch == 0 && key < Lk) {
+          sw += xb[jkey];
+          sb += xb[TK + jkey];
+          sc += xb[2 * TK + jkey];
+          const float vn = vn_s[i * TK + jkey] + vn_s[(TMAX + i) * TK + jkey];
+          p.scores[(size_t)h * Lk + key] = (sw * vn - 2.f * sb + sc) / (float)p.g;
+        }
+      }
+      stamp(rd, TR_PASS2);
+    }
+  }
+
+  // ---- teardown: every MMA finished (MMA lane waited on B_FIN), TMEM released --
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == WARP_MMA) tc::tmem_dealloc(tmem, 512);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Host planning and launch
+// ---------------------------------------------------------------------------
+struct TcPlan {
+  bool ok;
+  int npad, tmax, tiles, gs, groups, rounds, nctas;
+  size_t off_ctr, off_status, off_trace, off_pm, off_ps, off_py, off_y, off_lse, bytes;
+};
+
+static int tc_npad(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0; }
+
+TcPlan plan_tc(int BH, int Lk, int M, int D, int nsm) {
+  TcPlan t;
+  std::memset(&t, 0, sizeof(t));
+  t.npad = tc_npad(M);
+  if (!t.npad || (D != 64 && D != 128)) return t;
+  t.tmax = (512 - 2 * t.npad) / t.npad;
+  t.tiles = (Lk + TK - 1) / TK;
+  const int gs_min = (t.tiles + t.tmax - 1) / t.tmax;
+  if (gs_min > nsm) return t;
+  double best = 1e30;
+  for (int gs = gs_min; gs <= std::min(t.tiles, nsm); ++gs) {
+    int groups = std::min(nsm / gs, BH);
+    int rounds = (BH + groups - 1) / groups;
+    int per = (t.tiles + gs - 1) / gs;
+    double cost = rounds * (per + 3.0);  // ~3 tile-times of barrier/merge per round
+    if (cost < best - 1e-9) {
+      best = cost;
+      t.gs = gs;
+      t.groups = groups;
+      t.rounds = rounds;
+    }
+  }
+  if (t.gs > kMaxGs) return t;
+  t.nctas = t.gs * t.groups;
+  size_t off = 0;
+  t.off_ctr = off; off = align_up(off + (size_t)2 * BH * 4, 256);
+  t.off_status = off; off = align_up(off + 4, 256);
+  t.off_trace = off; off = align_up(off + 8 * (3 + (size_t)t.nctas * t.rounds * kTraceEv), 256);
+  t.off_pm = off; off = align_up(off + (size_t)BH * t.gs * M * 4, 256);
+  t.off_ps = off; off = align_up(off + (size_t)BH * t.gs * M * 4, 256);
+  t.off_py = off; off = align_up(off + (size_t)BH * t.gs * M * D * 4, 256);
+  t.off_y = off; off = align_up(off + (size_t)BH * M * D * 4, 256);
+  t.off_lse = off; off = align_up(off + (size_t)BH * M * 4, 256);
+  t.bytes = off;
+  t.ok = true;
+  return t;
+}
+
+template <typename T, int D, int NPAD, int ROUND>
+static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cudaStream_t st) {
+  constexpr int NS = (D == 128) ? (NPAD == 64 ? 3 : 4) : (NPAD == 64 ? 4 : 6);
+  using L = Lay<D, NPAD, NS>;
+  static_assert(L::ALLOC <= 232448, "shared memory budget");
+  CUtensorMap km, vm;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  const int BH = p.B * p.Hkv;
+  int rc = make_kv_tensor_map(&km, p.k, BH, p.Lk, D, bf16);
+  if (rc) return rc;
+  rc = make_kv_tensor_map(&vm, p.v, BH, p.Lk, D, bf16);
+  if (rc) return rc;
+  char* base = reinterpret_cast<char*>(ws);
+  TcArgs a;
+  a.p = p;
+  a.BH = BH;
+  a.gs = t.gs; a.groups = t.groups; a.rounds = t.rounds; a.tiles = t.tiles; a.tmax = t.tmax;
+  a.c = (float)(1.4426950408889634 / std::sqrt((double)p.D));
+  a.pscale = bf16 ? 1.0f : 32768.0f;
+  a.ctr = reinterpret_cast<int*>(base + t.off_ctr);
+  a.status = reinterpret_cast<int*>(base + t.off_status);
+  a.trace = reinterpret_cast<unsigned long long*>(base + t.off_trace);
+  a.part_m = reinterpret_cast<float*>(base + t.off_pm);
+  a.part_s = reinterpret_cast<float*>(base + t.off_ps);
+  a.part_y = reinterpret_cast<float*>(base + t.off_py);
+  a.y_g = reinterpret_cast<float*>(base + t.off_y);
+  a.lse_g = reinterpret_cast<float*>(base + t.off_lse);
+  if (cudaMemsetAsync(base + t.off_ctr, 0, t.off_pm - t.off_ctr, st) != cudaSuccess)
+    return fail(DROPKV_ERR_CUDA, "memset of barrier counters failed");
+  auto kern = fused_scores_kernel<T, D, NPAD, NS, ROUND>;
+  static unsigned long long attr_done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !(attr_done & (1ull << dev))) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess)
+      return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %d", L::ALLOC);
+    if (dev < 64) attr_done |= (1ull << dev);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(t.nctas);
+  cfg.blockDim = dim3(NTH);
+  cfg.dynamicSmemBytes = L::ALLOC;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, km, vm, a);
+  if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "fused scorer launch: %s", cudaGetErrorString(e));
+  return check_launch("fused_scores", 2);
+}
+
+bool tc_supported(int dtype, int M, int D, int BH, int Lk) {
+  if (dtype != DROPKV_DTYPE_BF16 && dtype != DROPKV_DTYPE_F16) return false;
+  TcPlan t = plan_tc(BH, Lk, M, D, num_sms_current_device());
+  return t.ok;
+}
+
+size_t tc_workspace_bytes(int M, int D, int BH, int Lk) {
+  TcPlan t = plan_tc(BH, Lk, M, D, num_sms_current_device());
+  return t.ok ? t.bytes : 0;
+}
+
+size_t tc_status_offset(int M, int D, int BH, int Lk) {
+  TcPlan t = plan_tc(BH, Lk, M, D, num_sms_current_device());
+  return t.off_status;
+}
+
+int launch_scores_tc(const ScoreProblem& p, int dtype, void* ws, cudaStream_t st) {
+  const int BH = p.B * p.Hkv;
+  TcPlan t = plan_tc(BH, p.Lk, p.M, p.D, num_sms_current_device());
+  if (!t.ok) return fail(DROPKV_ERR_UNSUPPORTED, "tensor-core scorer does not cover this shape");
+  const bool bf = dtype == DROPKV_DTYPE_BF16;
+  const bool rnd = p.round_mode != DROPKV_ROUND_NONE;
+#define DKV_CASE(TT, DD, NN, RR)                      \
+  if (p.D == DD && t.npad == NN && rnd == (RR != 0)) \
+    return launch_fused_t<TT, DD, NN, RR>(p, t, ws, st);
+#define DKV_SHAPES(TT, RR) \
+  DKV_CASE(TT, 128, 16, RR) DKV_CASE(TT, 128, 32, RR) DKV_CASE(TT, 128, 64, RR) \
+  DKV_CASE(TT, 64, 16, RR) DKV_CASE(TT, 64, 32, RR) DKV_CASE(TT, 64, 64, RR)
+  if (bf) {
+    DKV_SHAPES(__nv_bfloat16, 0)
+    DKV_SHAPES(__nv_bfloat16, DROPKV_ROUND_BF16)
+  } else {
+    DKV_SHAPES(__half, 0)
+    DKV_SHAPES(__half, DROPKV_ROUND_F16)
+  }
+#undef DKV_SHAPES
+#undef DKV_CASE
+  return fail(DROPKV_ERR_UNSUPPORTED, "no tensor-core kernel for D=%d, M=%d", p.D, p.M);
+}
+
+}  // namespace dropkv

@@ -14,10 +14,15 @@
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
 from . import _lib
+
+# With DROPKV_CHECK_STATUS=1 every scoring call synchronises and reads the device
+# status word of the tensor-core scorer (non-zero: a bounded wait timed out).
+_CHECK_STATUS = os.environ.get("DROPKV_CHECK_STATUS", "0") not in ("", "0")
 
 _DTYPE_CODE = {torch.float32: _lib.DTYPE_F32, torch.float16: _lib.DTYPE_F16,
                torch.bfloat16: _lib.DTYPE_BF16}
@@ -34,6 +39,21 @@ def _require_cuda(*ts):
 
 def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check_status(ws: torch.Tensor, dtype_code: int, B, Hq, Hkv, Lk, D, window, what: str):
+    off = _lib.load().dropkv_scores_status_offset(dtype_code, B, Hq, Hkv, Lk, D, int(window))
+    if off == _lib.NO_STATUS:
+        return
+    st = int(ws[off:off + 4].view(torch.int32).item())
+    if st != 0:
+        raise _lib.DropKVError(_lib.ERR_DEVICE, f"{what}: device status {st} (a bounded wait timed out)")
+
+
+def scorer_for(dtype: torch.dtype, B, Hq, Hkv, Lk, D, window) -> str:
+    """'tensor_cores' or 'cuda_cores': which scorer serves this problem."""
+    r = _lib.load().dropkv_scorer_for(_DTYPE_CODE[dtype], B, Hq, Hkv, Lk, D, int(window))
+    return {1: "cuda_cores", 2: "tensor_cores"}.get(r, "invalid")
 
 
 def _workspace(nbytes: int, device) -> torch.Tensor:
@@ -68,6 +88,8 @@ def scores(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int, eps: 
                                _ROUND_CODE[Q.dtype] if round_p else _lib.ROUND_NONE,
                                out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
         _lib.check(rc, "dropkv_scores")
+        if _CHECK_STATUS:
+            _check_status(ws, dt, B, Hq, Hkv, Lk, D, window, "dropkv_scores")
     return out
 
 
@@ -180,6 +202,8 @@ def compress(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int, ker
                                  idx.data_ptr(), Kc.data_ptr(), Vc.data_ptr(),
                                  ws.data_ptr(), ws.numel(), _stream(dev))
         _lib.check(rc, "dropkv_compress")
+        if _CHECK_STATUS:
+            _check_status(ws, dt, B, Hq, Hkv, Lk, D, window, "dropkv_compress")
     if return_scores:
         return idx, Kc, Vc, sc
     return idx, Kc, Vc

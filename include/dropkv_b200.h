@@ -82,6 +82,22 @@ DROPKV_API int dropkv_scores(const void* q, int64_t q_sb, int64_t q_sh, int64_t 
                   int window, float eps, int round_p, float* scores,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* Which scorer serves this problem: 2 = fused tensor-core kernel (tcgen05 +
+ * TMA; bf16/fp16, D in {64,128}, g*window <= 64), 1 = CUDA-core split-K kernels
+ * (every other supported problem).  0 for invalid sizes. */
+DROPKV_API int dropkv_scorer_for(int dtype, int B, int Hq, int Hkv, int Lk, int D, int window);
+
+/* Process-wide scorer selection: 0 = automatic (default), 1 = always the
+ * CUDA-core kernels, 2 = always the tensor-core kernel (calls it does not cover
+ * fail with DROPKV_ERR_UNSUPPORTED).  For testing one path against the other. */
+DROPKV_API int dropkv_set_scorer(int mode);
+
+/* Byte offset, inside a dropkv_scores / dropkv_compress workspace, of the int32
+ * device status word the tensor-core scorer writes (0 = every bounded wait
+ * completed; non-zero = a wait timed out and the results are invalid).
+ * (size_t)-1 when the problem runs on the CUDA-core kernels. */
+DROPKV_API size_t dropkv_scores_status_offset(int dtype, int B, int Hq, int Hkv, int Lk, int D, int window);
+
 /* Scratch bytes dropkv_select needs. */
 DROPKV_API size_t dropkv_select_workspace_size(int B, int Hkv, int Lk);
 
@@ -110,6 +126,16 @@ DROPKV_API int dropkv_compress(const void* q, int64_t q_sb, int64_t q_sh, int64_
                     int window, float eps, int round_p, int kernel_size, int protect_window,
                     int keep_len, float* scores_out, int64_t* keep_idx, void* k_out, void* v_out,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Diagnostic: one 128-row tile through a tcgen05 MMA form used by the fused
+ * scorer (mode 0: out[128][n] = A[128][128] B[n][128]^T with A loaded by TMA;
+ * mode 1: out[128][n] = A[128][128]^T B[n][128]^T with A read MN-major; modes 2/3:
+ * the same with 64-wide A rows).  a, b bf16 row-major; out fp32 [128][n];
+ * *status (device int, zeroed by the caller) becomes non-zero if a wait timed out.
+ * No counterpart in the reference: a hardware check of this library's building
+ * blocks. */
+DROPKV_API int dropkv_selftest_tcgen05(int mode, const void* a, const void* b, int n, float* out,
+                                       int* status, void* stream);
 
 #ifdef __cplusplus
 }

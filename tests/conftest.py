@@ -1,6 +1,9 @@
 import os
 import sys
 
+# Tests read the tensor-core scorer's device status word after every call.
+os.environ.setdefault("DROPKV_CHECK_STATUS", "1")
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 for p in (HERE, ROOT):
