@@ -5,30 +5,31 @@
 // of `gs` CTAs; group g scores heads g, g + groups, ... one round at a time, and
 // CTA `rank` of a group owns a contiguous range of <= tmax 128-key tiles of the
 // round's head.  Warp roles inside a CTA (coupled only through mbarriers):
-//   warp 8     TMA producer: K, V, V tiles of every round into an NS-slot ring;
-//   warp 9     MMA issuer (one thread) and TMEM owner;
-//   warps 0-7  epilogue: warp w reads TMEM lanes 32*(w%4).. (32 keys of a tile)
-//              and query columns [(w/4)*N/2, (w/4+1)*N/2).
+//   warp 16     TMA producer: K, V, V tiles of every round into an NS-slot ring;
+//   warp 17     MMA issuer (one thread) and TMEM owner;
+//   warps 0-15  epilogue: warp w reads TMEM lanes 32*(w%4).. (32 keys of a tile)
+//               and query columns [(w/4)*N/4, (w/4+1)*N/4).
 // Per head and CTA:
 //
 //   pass 1  K tiles stream in by TMA (L2 evict-first); tcgen05 computes the logit
 //           tile S = K Q^T (keys on the MMA M axis, the M query rows on N) into
 //           TMEM, where it stays for pass 2.  The CTA-local softmax max m and sum s
 //           per query row follow from the TMEM tiles; p = exp(l - m) is split into
-//           bf16/fp16 hi + lo halves in shared memory and V tiles (TMA, L2
-//           evict-last so pass 2 finds them in L2) give y^T += V^T p_hi^T + V^T p_lo^T
-//           (fp32 accumulation in TMEM: y keeps ~16 mantissa bits of p).
-//           The partial (m, s, y) goes to global memory.
+//           bf16/fp16 hi + lo halves in shared memory (MN-major: a row per key) and
+//           V tiles (TMA, L2 evict-last so pass 2 finds them in L2) give
+//           y^T += V^T p_hi^T + V^T p_lo^T (fp32 accumulation in TMEM: y keeps
+//           ~16 mantissa bits of p).  The partial (m, s, y) goes to global memory.
 //   merge   group barrier; each CTA merges a 1/gs slice of the head's M x D
 //           elements of y with the max-rescale rule (dropkv_triton.py:441-452),
 //           plus lse; group barrier.
 //   pass 2  y is split hi + lo into shared memory; V tiles come back by TMA
 //           (L2 hits); tcgen05 gives <v_j, y_m> = V (y_hi + y_lo)^T in TMEM; the
-//           epilogue (one thread per key, all M rows in registers) forms
+//           epilogue forms ||v_j||^2 from the V tile still in the ring, and
 //           p = exp(l - lse) clamped to [0,1] (rounded to the input dtype when
 //           requested), w = (p / (1 - p + eps))^2 and
 //           score_j = (sum w ||v_j||^2 - 2 sum w <v_j,y_m> + sum w ||y_m||^2) / g,
-//           the reference's termA - termB + termC (dropkv_triton.py:94-108).
+//           the reference's termA - termB + termC (dropkv_triton.py:94-108); the
+//           four column groups of a key combine their sums in a fixed order.
 //
 // Group barriers are bounded spins on global counters (zeroed by the host before
 // the launch); every wait in the kernel gives up after a timeout, records a
@@ -80,12 +81,13 @@ int make_kv_tensor_map(CUtensorMap* map, const void* base, int BH, int L, int D,
 namespace {
 
 constexpr int TK = 128;                      // keys per tile = MMA M
-constexpr int NEPI = 256;                    // epilogue threads (warps 0-7)
-constexpr int NTH = NEPI + 64;               // + TMA producer warp (8) + MMA warp (9)
-constexpr int WARP_TMA = 8, WARP_MMA = 9;
+constexpr int NEPI = 512;                    // epilogue threads (warps 0-15)
+constexpr int NEW = NEPI / 32;               // epilogue warps
+constexpr int NTH = NEPI + 64;               // + TMA producer warp + MMA warp
+constexpr int WARP_TMA = NEW, WARP_MMA = NEW + 1;
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
 constexpr int kMaxGs = 256;                  // CTAs per head group (at most)
-constexpr int kWts = 1024;                   // merge-weight buffer (floats)
+constexpr int kWts = 1024;                   // merge maxima / sums buffers (floats each)
 constexpr int kMaxTiles = 30;                // TMEM logit tiles per CTA and head (N = 16)
 
 struct TcArgs {
@@ -108,35 +110,40 @@ struct TcArgs {
 // trace[3 + (cta * rounds + round) * kTraceEv + ev]; trace[0..2] = {ctas, rounds, kTraceEv}.
 enum { TR_START, TR_LOGITS, TR_MAX, TR_PV, TR_BAR_A, TR_MERGE, TR_BAR_B, TR_YSTAGE, TR_PASS2, kTraceEv };
 
-template <int D, int NPAD, int NS>
+// mbarrier indices after full[NS], free[NS] and s_done[kMaxTiles]
+enum {
+  B_QREADY = 0, B_PREADY0, B_PREADY1, B_PFREE0, B_PFREE1, B_YDONE, B_YREADY,
+  B_S2READY0, B_S2READY1, B_S2FREE0, B_S2FREE1, B_FIN, kAuxBars
+};
+
+// Shared-memory layout.  Q and y are K-major SW128 operands (NPAD rows of 64
+// elements per 128-byte region row); P tiles are MN-major: one row per key holding
+// its NPAD query columns (2 * NPAD bytes, swizzled at that width), which is the
+// layout an epilogue thread owning one key writes with vector stores.
+template <int D, int NPAD, int NS, int NPB>
 struct Lay {
   static constexpr int TILE = TK * D * 2;         // one K or V tile
   static constexpr int RB = NPAD * 128;           // one SW128 region of NPAD rows
+  static constexpr int PRB = 2 * NPAD;            // bytes per key row of a P tile
+  static constexpr int PT = TK * PRB;             // one P tile (hi or lo half)
   static constexpr int TMAX = (512 - 2 * NPAD) / NPAD;
   static constexpr int RING = 0;
   static constexpr int QS = RING + NS * TILE;     // D/64 regions
-  static constexpr int PS = QS + (D / 64) * RB;   // [buf 2][hi/lo 2][key half 2] regions
-  static constexpr int YS = PS + 8 * RB;          // [hi/lo 2][D/64] regions
+  static constexpr int PS = QS + (D / 64) * RB;   // [NPB buffers][hi/lo] P tiles
+  static constexpr int YS = PS + NPB * 2 * PT;    // [hi/lo][D/64] regions
   static constexpr int FL = YS + 2 * (D / 64) * RB;
   static constexpr int MLOC = FL;                 // floats [NPAD]
   static constexpr int LSE = MLOC + 4 * NPAD;
   static constexpr int YN = LSE + 4 * NPAD;
   static constexpr int BND = YN + 4 * NPAD;       // int [NPAD] causal bound per row
-  static constexpr int RED = BND + 4 * NPAD;      // [8 warps][NPAD]
-  static constexpr int XCH = RED + 32 * NPAD;     // [2 buf][3][TK] pass-2 half exchange
-  static constexpr int WTS = XCH + 4 * 6 * TK;    // [kWts]
-  static constexpr int VN = WTS + 4 * kWts;       // [2 halves][TMAX][TK]
-  static constexpr int BAR = VN + 8 * TMAX * TK;  // mbarriers
-  static constexpr int NBAR = 2 * NS + kMaxTiles + 12;
+  static constexpr int RED = BND + 4 * NPAD;      // [4 lane quadrants][NPAD]
+  static constexpr int XCH = RED + 16 * NPAD;     // [2 buf][3 column groups][4 sums][TK]
+  static constexpr int WTS = XCH + 4 * 24 * TK;   // [2][kWts]
+  static constexpr int BAR = WTS + 8 * kWts;      // mbarriers
+  static constexpr int NBAR = 2 * NS + kMaxTiles + kAuxBars;
   static constexpr int MISC = BAR + 8 * NBAR;     // tmem slot, flags
   static constexpr int BYTES = MISC + 64;
   static constexpr int ALLOC = BYTES + 1024;      // + alignment slack
-};
-
-// mbarrier indices after full[NS], free[NS] and s_done[kMaxTiles]
-enum {
-  B_QREADY = 0, B_PREADY0, B_PREADY1, B_PFREE0, B_PFREE1, B_YDONE, B_YREADY,
-  B_S2READY0, B_S2READY1, B_S2FREE0, B_S2FREE1, B_FIN, kAuxBars
 };
 
 template <typename T>
@@ -158,6 +165,30 @@ __device__ __forceinline__ float from_bits<__nv_bfloat16>(uint16_t b) {
 template <>
 __device__ __forceinline__ float from_bits<__half>(uint16_t b) {
   return __half2float(__ushort_as_half(b));
+}
+
+// Two floats rounded to T and packed (x in the low half), and back.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float x, float y);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float x, float y) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float x, float y) {
+  __half2 h = __floats2half2_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t u);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t u) {
+  return __half22float2(*reinterpret_cast<__half2*>(&u));
 }
 
 template <int ROUND>
@@ -191,34 +222,62 @@ __device__ __forceinline__ float col_reduce(float (&v)[C], int lane) {
   return r;
 }
 
-// TMEM -> registers, C fp32 columns of this thread's lane (C in {8, 16, 32}).
+// TMEM -> registers, C fp32 columns of this thread's lane (C in {4, 8, 16}).
 template <int C>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v);
-template <>
-__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float* v) { tc::tmem_ld32(taddr, v); }
 template <>
 __device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float* v) { tc::tmem_ld16(taddr, v); }
 template <>
 __device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, float* v) { tc::tmem_ld8(taddr, v); }
+template <>
+__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, float* v) { tc::tmem_ld4(taddr, v); }
 
-__device__ __forceinline__ void epi_sync() {  // named barrier of the 256 epilogue threads
+__device__ __forceinline__ void epi_sync() {  // named barrier of the epilogue threads
   asm volatile("bar.sync 1, %0;" ::"r"(NEPI) : "memory");
 }
-__device__ __forceinline__ void pair_sync(int q) {  // the two warps of TMEM quadrant q
-  asm volatile("bar.sync %0, 64;" ::"r"(2 + q) : "memory");
+__device__ __forceinline__ void quad_sync(int q) {  // the four warps of TMEM lane quadrant q
+  asm volatile("bar.sync %0, 128;" ::"r"(2 + q) : "memory");
 }
 
-template <typename T, int D, int NPAD, int NS, int ROUND>
+// HC query columns of one key as hi/lo halves of T, stored to the MN-major P tiles.
+template <typename T, int HC, int PRB>
+__device__ __forceinline__ void store_p(uint8_t* hi_tile, uint8_t* lo_tile, int jkey, int cbase,
+                                        const float (&ps)[HC]) {
+  uint32_t hw[HC / 2], lw[HC / 2];
+#pragma unroll
+  for (int j = 0; j < HC; j += 2) {
+    hw[j / 2] = pack2<T>(ps[j], ps[j + 1]);
+    const float2 back = unpack2<T>(hw[j / 2]);
+    lw[j / 2] = pack2<T>(ps[j] - back.x, ps[j + 1] - back.y);
+  }
+  if constexpr (HC == 4) {
+    const uint32_t off = tc::swz_offset<PRB>(jkey, cbase);
+    *reinterpret_cast<uint2*>(hi_tile + off) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(lo_tile + off) = make_uint2(lw[0], lw[1]);
+  } else {
+#pragma unroll
+    for (int c8 = 0; c8 < HC / 8; ++c8) {
+      const uint32_t off = tc::swz_offset<PRB>(jkey, cbase + 8 * c8);
+      *reinterpret_cast<uint4*>(hi_tile + off) = make_uint4(hw[4 * c8], hw[4 * c8 + 1], hw[4 * c8 + 2], hw[4 * c8 + 3]);
+      *reinterpret_cast<uint4*>(lo_tile + off) = make_uint4(lw[4 * c8], lw[4 * c8 + 1], lw[4 * c8 + 2], lw[4 * c8 + 3]);
+    }
+  }
+}
+
+template <typename T, int D, int NPAD, int NS, int NPB, int ROUND>
 __global__ void __launch_bounds__(NTH, 1)
     fused_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                         TcArgs a) {
-  using L = Lay<D, NPAD, NS>;
+  using L = Lay<D, NPAD, NS, NPB>;
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int NREG = D / 64;            // 64-wide slabs of a K/V/Q/Y row
   constexpr int TMAX = L::TMAX;
   constexpr int S2COL = TMAX * NPAD;      // y^T accumulator / S2 buffer 0; buffer 1 follows
-  constexpr int HC = NPAD / 2;            // query columns per epilogue warp
+  constexpr int HC = NPAD / 4;            // query columns per epilogue warp
+  constexpr int PRB = L::PRB;
+  constexpr int EPC = D / 4;              // V-row elements per column group (||v||^2)
   static_assert(TMAX <= kMaxTiles, "s_done barriers");
+  static_assert(HC >= 4 && HC <= 16, "column split");
   extern __shared__ uint8_t raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::BAR);
@@ -234,7 +293,7 @@ __global__ void __launch_bounds__(NTH, 1)
   float* red = reinterpret_cast<float*>(sm + L::RED);
   float* xch = reinterpret_cast<float*>(sm + L::XCH);
   float* wts = reinterpret_cast<float*>(sm + L::WTS);
-  float* vn_s = reinterpret_cast<float*>(sm + L::VN);
+  float* sts = wts + kWts;
 
   const ScoreProblem& p = a.p;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -246,11 +305,14 @@ __global__ void __launch_bounds__(NTH, 1)
 
   if (tid == 0) {
     for (int i = 0; i < L::NBAR; ++i) tc::mbar_init(&full[i], 1);
-    // multi-arrival barriers: one arrival per epilogue warp
-    tc::mbar_init(&bx[B_PREADY0], 8);
-    tc::mbar_init(&bx[B_PREADY1], 8);
-    tc::mbar_init(&bx[B_S2FREE0], 8);
-    tc::mbar_init(&bx[B_S2FREE1], 8);
+    // a ring slot is free after its MMA (commit) and one arrival per epilogue warp;
+    // for K and pass-1 V tiles, which the epilogue never reads, the MMA thread
+    // makes those arrivals itself
+    for (int s = 0; s < NS; ++s) tc::mbar_init(&freeb[s], 1 + NEW);
+    tc::mbar_init(&bx[B_PREADY0], NEW);
+    tc::mbar_init(&bx[B_PREADY1], NEW);
+    tc::mbar_init(&bx[B_S2FREE0], NEW);
+    tc::mbar_init(&bx[B_S2FREE1], NEW);
     tc::fence_mbar_init();
     *abort_flag = 0;
     if (blockIdx.x == 0) {
@@ -301,7 +363,8 @@ __global__ void __launch_bounds__(NTH, 1)
       tc::tma_prefetch_desc(&kmap);
       tc::tma_prefetch_desc(&vmap);
       const uint32_t total = (uint32_t)my_rounds * 3u * (uint32_t)nt;
-      for (uint32_t k = 0; k < total; ++k) {
+      uint32_t k = 0;
+      for (; k < total; ++k) {
         const uint32_t slot = k % NS;
         if (k >= NS && !wait_bar(&freeb[slot], ((k / NS) - 1) & 1, 2)) break;
         const int r = (int)(k / (3u * nt));
@@ -313,6 +376,10 @@ __global__ void __launch_bounds__(NTH, 1)
           tc::tma_load_3d(sm + L::RING + slot * L::TILE + rr * 16384, stage == 0 ? &kmap : &vmap, &full[slot],
                           64 * rr, (t0 + tile) * TK, bh, stage == 1 ? pol_last : pol_first);
       }
+      // every issued copy has landed before the CTA may exit (already true unless
+      // a wait gave up)
+      for (uint32_t j = (k > (uint32_t)NS ? k - NS : 0u); j < k; ++j)
+        if (!tc::mbar_wait(&full[j % NS], (j / NS) & 1, kWaitNs)) atomicOr(a.status, 3);
     }
   } else if (warp == WARP_MMA) {
     // ======================= MMA issuer ========================================
@@ -322,8 +389,9 @@ __global__ void __launch_bounds__(NTH, 1)
       const uint32_t ps0 = tc::smem_addr(sm + L::PS);
       const uint32_t ys0 = tc::smem_addr(sm + L::YS);
       constexpr uint32_t ID_QK = tc::idesc_f16(BF16, 128, NPAD, false, false);
-      constexpr uint32_t ID_PV = tc::idesc_f16(BF16, 128, NPAD, true, false);
+      constexpr uint32_t ID_PV = tc::idesc_f16(BF16, 128, NPAD, true, true);
       constexpr uint32_t LBO_PV = (NREG == 2) ? 16384u : 0u;
+      constexpr uint32_t LAYOUT_P = tc::layout_for_row_bytes(PRB);
       uint32_t k = 0;  // ring position
       uint32_t c_pready[2] = {0, 0}, c_s2free[2] = {0, 0};
       for (int rd = 0; rd < my_rounds && !*vabort; ++rd) {
@@ -342,28 +410,30 @@ __global__ void __launch_bounds__(NTH, 1)
             tc::mma_f16(tmem + i * NPAD, ad, bd, ID_QK, kk > 0);
           }
           tc::mma_commit(&freeb[slot]);
+          tc::mbar_arrive_cnt(&freeb[slot], NEW);
           tc::mma_commit(&sdone[i]);
         }
         // pass 1c: y^T += V_i^T (p_hi + p_lo)^T
         for (int i = 0; i < nt; ++i, ++k) {
           const uint32_t slot = k % NS;
-          const int buf = i & 1;
+          const int buf = i % NPB;
           if (!wait_bar(&full[slot], (k / NS) & 1, 22)) break;
           if (!wait_bar(&bx[B_PREADY0 + buf], c_pready[buf] & 1, 23)) break;
           ++c_pready[buf];
           tc::tc_fence_after();
           const uint32_t a0 = ring0 + slot * L::TILE;
-          const uint32_t pb = ps0 + buf * 4 * L::RB;
+          const uint32_t pb = ps0 + buf * 2 * L::PT;
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
               const uint64_t ad = tc::smem_desc(a0 + kk * 2048, LBO_PV, 1024);
-              const uint64_t bd = tc::smem_desc(pb + half * 2 * L::RB + (kk / 4) * L::RB + (kk % 4) * 32, 16, 1024);
+              const uint64_t bd = tc::smem_desc(pb + half * L::PT + kk * 16 * PRB, 0, 8 * PRB, LAYOUT_P);
               tc::mma_f16(tmem + S2COL, ad, bd, ID_PV, (i > 0 || half > 0 || kk > 0) ? 1u : 0u);
             }
           }
           tc::mma_commit(&freeb[slot]);
+          tc::mbar_arrive_cnt(&freeb[slot], NEW);
           tc::mma_commit(&bx[B_PFREE0 + buf]);
         }
         tc::mma_commit(&bx[B_YDONE]);
@@ -389,7 +459,7 @@ __global__ void __launch_bounds__(NTH, 1)
               tc::mma_f16(tmem + S2COL + buf * NPAD, ad, bd, ID_QK, (half > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          tc::mma_commit(&freeb[slot]);
+          tc::mma_commit(&freeb[slot]);  // the epilogue warps add theirs after ||v||^2
           tc::mma_commit(&bx[B_S2READY0 + buf]);
         }
         // the last (up to two) S2 buffers are released after this round's epilogue
@@ -403,13 +473,13 @@ __global__ void __launch_bounds__(NTH, 1)
       if (!tc::mbar_wait(&bx[B_FIN], 0, kWaitNs)) atomicOr(a.status, 28);
     }
   } else {
-    // ======================= epilogue: warps 0-7 ==============================
+    // ======================= epilogue: warps 0-15 =============================
     const int q = warp & 3;              // TMEM lane quadrant: keys 32q .. 32q+31 of a tile
-    const int ch = warp >> 2;            // query-column half
-    const int et = tid;                  // 0 .. 255
+    const int cg = warp >> 2;            // query-column group
+    const int et = tid;                  // 0 .. NEPI-1
     const int jkey = q * 32 + lane;      // key within a tile
     const uint32_t lrow = (uint32_t)(q * 32) << 16;
-    const int cbase = ch * HC;
+    const int cbase = cg * HC;
     uint32_t c_pfree[2] = {0, 0}, c_s2r[2] = {0, 0};
     const bool stamper = (et == 0);
     auto stamp = [&](int rd, int ev) {
@@ -478,7 +548,7 @@ __global__ void __launch_bounds__(NTH, 1)
       epi_sync();
       stamp(rd, TR_MAX);
 
-      // ---- pass 1c: p = exp2(l - m) -> hi/lo P tiles; ||v||^2 -------------------
+      // ---- pass 1c: p = exp2(l - m) -> hi/lo P tiles -----------------------------
       float ssum[HC];
 #pragma unroll
       for (int j = 0; j < HC; ++j) ssum[j] = 0.f;
@@ -486,10 +556,8 @@ __global__ void __launch_bounds__(NTH, 1)
 #pragma unroll
       for (int j = 0; j < HC; ++j) ml[j] = mloc[cbase + j];
       for (int i = 0; i < nt; ++i) {
-        const int buf = i & 1;
-        const uint32_t kpos = (uint32_t)rd * 3u * nt + nt + i;  // ring position of V tile i
-        const uint32_t slot = kpos % NS;
-        if (i >= 2) {
+        const int buf = i % NPB;
+        if (i >= NPB) {
           wait_bar(&bx[B_PFREE0 + buf], c_pfree[buf] & 1, 31);
           ++c_pfree[buf];
         }
@@ -498,43 +566,16 @@ __global__ void __launch_bounds__(NTH, 1)
         tmem_ld<HC>(tmem + lrow + i * NPAD + cbase, s);
         const int key = (t0 + i) * TK + jkey;
         const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
-        uint8_t* pb = sm + L::PS + buf * 4 * L::RB + (jkey >> 6) * L::RB;
+        float ps[HC];
 #pragma unroll
         for (int j = 0; j < HC; ++j) {
-          const int m = cbase + j;
-          const bool ok = (edge ? (key <= bnd_s[m] && key < Lk) : colok[j]) && ml[j] != -INFINITY;
+          const bool ok = (edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j]) && ml[j] != -INFINITY;
           const float pr = ok ? exp2f(fmaf(s[j], a.c, -ml[j])) : 0.f;
           ssum[j] += pr;
-          const float ps = pr * a.pscale;
-          const uint16_t hi = to_bits<T>(ps);
-          const uint16_t lo = to_bits<T>(ps - from_bits<T>(hi));
-          const uint32_t off = tc::sw128_offset(m, jkey & 63);
-          *reinterpret_cast<uint16_t*>(pb + off) = hi;
-          *reinterpret_cast<uint16_t*>(pb + 2 * L::RB + off) = lo;
+          ps[j] = pr * a.pscale;
         }
-        // V tile i: read it for ||v||^2 before it may be released (the P.V MMA
-        // runs only after every warp's p_ready arrival below)
-        wait_bar(&full[slot], (kpos / NS) & 1, 32);
-        // ||v_j||^2, this warp's 64-wide slab of the row (D = 64: half 1 has none)
-        {
-          float acc = 0.f;
-          if (ch < NREG) {
-            const uint8_t* vt = sm + L::RING + slot * L::TILE + ch * 16384 + jkey * 128;
-#pragma unroll
-            for (int c8 = 0; c8 < 8; ++c8) {
-              const uint4 r4 = *reinterpret_cast<const uint4*>(vt + ((c8 ^ (jkey & 7)) << 4));
-              const uint32_t w4[4] = {r4.x, r4.y, r4.z, r4.w};
-#pragma unroll
-              for (int k2 = 0; k2 < 4; ++k2) {
-                const float x0 = from_bits<T>((uint16_t)(w4[k2] & 0xffffu));
-                const float x1 = from_bits<T>((uint16_t)(w4[k2] >> 16));
-                acc = fmaf(x0, x0, acc);
-                acc = fmaf(x1, x1, acc);
-              }
-            }
-          }
-          vn_s[(ch * TMAX + i) * TK + jkey] = acc;
-        }
+        uint8_t* pb = sm + L::PS + buf * 2 * L::PT;
+        store_p<T, HC, PRB>(pb, pb + L::PT, jkey, cbase, ps);
         tc::fence_proxy_async_smem();
         tc::tc_fence_before();
         __syncwarp();
@@ -542,9 +583,9 @@ __global__ void __launch_bounds__(NTH, 1)
       }
       // y^T complete
       if (nt > 0) wait_bar(&bx[B_YDONE], rd & 1, 33);
-      // the P buffers of the last one or two tiles were released by that too
-      for (int i = (nt >= 2 ? nt - 2 : 0); i < nt; ++i) {
-        const int buf = i & 1;
+      // the P buffers of the last tiles were released by that too
+      for (int i = (nt >= NPB ? nt - NPB : 0); i < nt; ++i) {
+        const int buf = i % NPB;
         wait_bar(&bx[B_PFREE0 + buf], c_pfree[buf] & 1, 34);
         ++c_pfree[buf];
       }
@@ -597,45 +638,41 @@ __global__ void __launch_bounds__(NTH, 1)
       group_barrier(a.ctr + 2 * h);
       stamp(rd, TR_BAR_A);
       {
+        // This CTA merges elements [e0, e1) of the head's M x D y with the
+        // max-rescale rule (dropkv_triton.py:441-452), in a fixed order.
         const int E = M * D;
         const int e0 = (int)(((long long)rank * E) / a.gs), e1 = (int)(((long long)(rank + 1) * E) / a.gs);
         const int ne = e1 - e0;
         const size_t hb = (size_t)h * a.gs;
-        float* acc = reinterpret_cast<float*>(sm + L::PS);  // P buffers are idle here
+        float* acc = reinterpret_cast<float*>(sm + L::PS);  // P tiles are idle here
+        constexpr int CAP = NPB * 2 * L::PT / 4;            // floats
         if (ne > 0) {
           const int m_lo = e0 / D, nrow = (e1 - 1) / D - m_lo + 1;
-          const int npairs = a.gs * ne;
           const int nst = nrow * a.gs;
-          float* sts = acc + npairs;  // part_s of the slice rows
-          // one round trip: maxima, sums and every (partial, element) value of the slice
-          for (int k0 = 0; k0 < npairs + 2 * nst; k0 += 8 * NEPI) {
-            float val[8];
+          // partial maxima and sums of the slice's rows, all loads in flight together
+          for (int k0 = 0; k0 < 2 * nst; k0 += 4 * NEPI) {
+            float val[4];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 4; ++u) {
               const int k = k0 + u * NEPI + et;
               val[u] = 0.f;
-              if (k < npairs) {
-                const int c = k / ne, e = k % ne;
-                const int eg = e0 + e, m = eg / D, d = eg % D;
-                val[u] = __ldcg(a.part_y + ((hb + c) * M + m) * D + d);
-              } else if (k < npairs + nst) {
-                const int kk = k - npairs, r = kk / a.gs, c = kk % a.gs;
+              if (k < nst) {
+                const int r = k / a.gs, c = k % a.gs;
                 val[u] = __ldcg(a.part_m + (hb + c) * M + m_lo + r);
-              } else if (k < npairs + 2 * nst) {
-                const int kk = k - npairs - nst, r = kk / a.gs, c = kk % a.gs;
+              } else if (k < 2 * nst) {
+                const int kk = k - nst, r = kk / a.gs, c = kk % a.gs;
                 val[u] = __ldcg(a.part_s + (hb + c) * M + m_lo + r);
               }
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 4; ++u) {
               const int k = k0 + u * NEPI + et;
-              if (k < npairs) acc[k] = val[u];
-              else if (k < npairs + nst) wts[k - npairs] = val[u];
-              else if (k < npairs + 2 * nst) sts[k - npairs - nst] = val[u];
+              if (k < nst) wts[k] = val[u];
+              else if (k < 2 * nst) sts[k - nst] = val[u];
             }
           }
           epi_sync();
-          for (int r = warp; r < nrow; r += NEPI / 32) {
+          for (int r = warp; r < nrow; r += NEW) {
             float mxr = -INFINITY;
             for (int c = lane; c < a.gs; c += 32) mxr = fmaxf(mxr, wts[r * a.gs + c]);
 #pragma unroll
@@ -655,25 +692,51 @@ __global__ void __launch_bounds__(NTH, 1)
             }
           }
           epi_sync();
-          // fixed-order weighted sums (deterministic); SPL threads per element
-          const int spl = max(1, min(8, 512 / ne));
-          for (int idx = et; idx < ne * spl; idx += NEPI) {
-            const int e = idx / spl, sp = idx % spl;
-            const int eg = e0 + e, m = eg / D;
-            const float* wr = wts + (m - m_lo) * a.gs;
-            float sacc = 0.f;
-            for (int c = sp; c < a.gs; c += spl) sacc = fmaf(wr[c], acc[c * ne + e], sacc);
-            if (spl == 1) __stcg(a.y_g + (size_t)h * E + eg, sacc / red[m - m_lo]);
-            else xch[idx] = sacc;
-          }
-          if (spl > 1) {
-            epi_sync();
-            for (int e = et; e < ne; e += NEPI) {
-              float sacc = 0.f;
-              for (int sp = 0; sp < spl; ++sp) sacc += xch[e * spl + sp];
-              const int eg = e0 + e, m = eg / D;
-              __stcg(a.y_g + (size_t)h * E + eg, sacc / red[m - m_lo]);
+          // weighted sums in chunks of elements whose partials fit the P tiles
+          const int ec = max(1, min(ne, CAP / a.gs));
+          for (int cs = 0; cs < ne; cs += ec) {
+            const int cn = min(ec, ne - cs);
+            const int npairs = a.gs * cn;
+            for (int k0 = 0; k0 < npairs; k0 += 8 * NEPI) {
+              float val[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const int k = k0 + u * NEPI + et;
+                val[u] = 0.f;
+                if (k < npairs) {
+                  const int c = k / cn, e = k % cn;
+                  const int eg = e0 + cs + e, m = eg / D, d = eg % D;
+                  val[u] = __ldcg(a.part_y + ((hb + c) * M + m) * D + d);
+                }
+              }
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const int k = k0 + u * NEPI + et;
+                if (k < npairs) acc[k] = val[u];
+              }
             }
+            epi_sync();
+            // SPL threads per element, each over a fixed subset of the partials
+            const int spl = max(1, min(8, NEPI / cn));
+            for (int idx = et; idx < cn * spl; idx += NEPI) {
+              const int e = idx / spl, sp = idx % spl;
+              const int eg = e0 + cs + e, m = eg / D;
+              const float* wr = wts + (m - m_lo) * a.gs;
+              float sacc = 0.f;
+              for (int c = sp; c < a.gs; c += spl) sacc = fmaf(wr[c], acc[c * cn + e], sacc);
+              if (spl == 1) __stcg(a.y_g + (size_t)h * E + eg, sacc / red[m - m_lo]);
+              else xch[idx] = sacc;
+            }
+            if (spl > 1) {
+              epi_sync();
+              for (int e = et; e < cn; e += NEPI) {
+                float sacc = 0.f;
+                for (int sp = 0; sp < spl; ++sp) sacc += xch[e * spl + sp];
+                const int eg = e0 + cs + e, m = eg / D;
+                __stcg(a.y_g + (size_t)h * E + eg, sacc / red[m - m_lo]);
+              }
+            }
+            epi_sync();  // acc and xch are refilled by the next chunk
           }
           if (et < nrow && e0 <= (m_lo + et) * D)
             __stcg(a.lse_g + (size_t)h * M + m_lo + et, red[NPAD + et] + log2f(red[et]));
@@ -708,11 +771,9 @@ __global__ void __launch_bounds__(NTH, 1)
             for (int k2 = 0; k2 < 8; k2 += 2) {
               n2 = fmaf(y[k2], y[k2], n2);
               n2 = fmaf(y[k2 + 1], y[k2 + 1], n2);
-              const uint16_t h0 = to_bits<T>(y[k2]), h1 = to_bits<T>(y[k2 + 1]);
-              const uint16_t l0 = to_bits<T>(y[k2] - from_bits<T>(h0));
-              const uint16_t l1 = to_bits<T>(y[k2 + 1] - from_bits<T>(h1));
-              hw[k2 / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-              lw[k2 / 2] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+              hw[k2 / 2] = pack2<T>(y[k2], y[k2 + 1]);
+              const float2 back = unpack2<T>(hw[k2 / 2]);
+              lw[k2 / 2] = pack2<T>(y[k2] - back.x, y[k2 + 1] - back.y);
             }
             const uint32_t off = (d / 64) * L::RB + m * 128 + ((((d % 64) >> 3) ^ (m & 7)) << 4);
             *reinterpret_cast<uint4*>(sm + L::YS + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
@@ -732,15 +793,18 @@ __global__ void __launch_bounds__(NTH, 1)
       if (et == 0) tc::mbar_arrive(&bx[B_YREADY]);
       stamp(rd, TR_YSTAGE);
 
-      // ---- pass 2: score epilogue over S (TMEM, pass 1) and S2 = <v, y> ------------
+      // ---- pass 2: score epilogue over S (TMEM, pass 1), S2 = <v, y> and ||v||^2 ----
       float lsel[HC], ynl[HC];
 #pragma unroll
       for (int j = 0; j < HC; ++j) {
         lsel[j] = lse_s[cbase + j];
         ynl[j] = yn_s[cbase + j];
       }
+      const int vslab = (cg * EPC) / 64, vc0 = ((cg * EPC) % 64) / 8;
       for (int i = 0; i < nt; ++i) {
         const int buf = i & 1;
+        const uint32_t kpos = (uint32_t)rd * 3u * nt + 2u * nt + i;  // ring position of V tile i
+        const uint32_t slot = kpos % NS;
         wait_bar(&bx[B_S2READY0 + buf], c_s2r[buf] & 1, 36);
         ++c_s2r[buf];
         tc::tc_fence_after();
@@ -750,6 +814,27 @@ __global__ void __launch_bounds__(NTH, 1)
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bx[B_S2FREE0 + buf]);
+        // ||v_j||^2 over this group's EPC elements of the row; the slot is held for
+        // this read by the arrival below (its full phase has completed: the S2 MMA
+        // read the tile)
+        wait_bar(&full[slot], (kpos / NS) & 1, 32);
+        float vn = 0.f;
+        {
+          const uint8_t* vt = sm + L::RING + slot * L::TILE + vslab * 16384 + jkey * 128;
+#pragma unroll
+          for (int c8 = 0; c8 < EPC / 8; ++c8) {
+            const uint4 r4 = *reinterpret_cast<const uint4*>(vt + (((vc0 + c8) ^ (jkey & 7)) << 4));
+            const uint32_t w4[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+            for (int k2 = 0; k2 < 4; ++k2) {
+              const float2 x = unpack2<T>(w4[k2]);
+              vn = fmaf(x.x, x.x, vn);
+              vn = fmaf(x.y, x.y, vn);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&freeb[slot]);
         const int key = (t0 + i) * TK + jkey;
         const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
         float sw = 0.f, sb = 0.f, sc = 0.f;
@@ -765,18 +850,25 @@ __global__ void __launch_bounds__(NTH, 1)
           sb = fmaf(w, s2[j], sb);
           sc = fmaf(w, ynl[j], sc);
         }
-        float* xb = xch + buf * 3 * TK;
-        if (ch == 1) {
-          xb[jkey] = sw;
-          xb[TK + jkey] = sb;
-          xb[2 * TK + jkey] = sc;
+        // column groups 1-3 hand their sums to group 0 (fixed order: deterministic)
+        float* xb = xch + buf * 12 * TK;
+        if (cg > 0) {
+          float* xg = xb + (cg - 1) * 4 * TK;
+          xg[jkey] = sw;
+          xg[TK + jkey] = sb;
+          xg[2 * TK + jkey] = sc;
+          xg[3 * TK + jkey] = vn;
         }
-        pair_sync(q);
-        if (ch == 0 && key < Lk) {
-          sw += xb[jkey];
-          sb += xb[TK + jkey];
-          sc += xb[2 * TK + jkey];
-          const float vn = vn_s[i * TK + jkey] + vn_s[(TMAX + i) * TK + jkey];
+        quad_sync(q);
+        if (cg == 0 && key < Lk) {
+#pragma unroll
+          for (int g3 = 0; g3 < 3; ++g3) {
+            const float* xg = xb + g3 * 4 * TK;
+            sw += xg[jkey];
+            sb += xg[TK + jkey];
+            sc += xg[2 * TK + jkey];
+            vn += xg[3 * TK + jkey];
+          }
           p.scores[(size_t)h * Lk + key] = (sw * vn - 2.f * sb + sc) / (float)p.g;
         }
       }
@@ -844,8 +936,10 @@ TcPlan plan_tc(int BH, int Lk, int M, int D, int nsm) {
 
 template <typename T, int D, int NPAD, int ROUND>
 static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cudaStream_t st) {
-  constexpr int NS = (D == 128) ? (NPAD == 64 ? 3 : 4) : (NPAD == 64 ? 4 : 6);
-  using L = Lay<D, NPAD, NS>;
+  // ring depth and P double-buffering as far as 227 KB of shared memory allows
+  constexpr int NS = (D == 128) ? (NPAD == 16 ? 5 : NPAD == 32 ? 4 : 3) : 8;
+  constexpr int NPB = (NPAD == 64) ? 1 : 2;
+  using L = Lay<D, NPAD, NS, NPB>;
   static_assert(L::ALLOC <= 232448, "shared memory budget");
   CUtensorMap km, vm;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -871,7 +965,7 @@ static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cuda
   a.lse_g = reinterpret_cast<float*>(base + t.off_lse);
   if (cudaMemsetAsync(base + t.off_ctr, 0, t.off_pm - t.off_ctr, st) != cudaSuccess)
     return fail(DROPKV_ERR_CUDA, "memset of barrier counters failed");
-  auto kern = fused_scores_kernel<T, D, NPAD, NS, ROUND>;
+  auto kern = fused_scores_kernel<T, D, NPAD, NS, NPB, ROUND>;
   static unsigned long long attr_done = 0;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -48,6 +48,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t byte
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(b)) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(count) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -170,6 +173,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 4 consecutive fp32 columns.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+  uint32_t r[4];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
 // 8 consecutive fp32 columns.
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
   uint32_t r[8];
@@ -186,18 +201,37 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
 // ---------------------------------------------------------------------------
 // Descriptors
 // ---------------------------------------------------------------------------
-constexpr uint32_t kLayoutSW128 = 2;  // tcgen05 descriptor layout code for 128-byte swizzle
+// tcgen05 descriptor layout codes (bits 61-63)
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW64 = 4;
+constexpr uint32_t kLayoutSW32 = 6;
+
+// Layout code for rows of `row_bytes` (32, 64 or 128) under the matching swizzle.
+__host__ __device__ constexpr uint32_t layout_for_row_bytes(int row_bytes) {
+  return row_bytes == 128 ? kLayoutSW128 : (row_bytes == 64 ? kLayoutSW64 : kLayoutSW32);
+}
+
+// Byte offset of 16-bit element e of row r in a region of `RB`-byte rows under the
+// RB-byte swizzle (RB in {32, 64, 128}): 16-byte chunk c of the row is XORed with
+// address bits 7.. of the row start, which is what TMA and the tensor core use.
+template <int RB>
+__host__ __device__ __forceinline__ uint32_t swz_offset(uint32_t r, uint32_t e) {
+  const uint32_t c = e >> 3;
+  const uint32_t sw = ((r * RB) >> 7) & (uint32_t)(RB / 16 - 1);
+  return r * RB + (((c ^ sw) << 4) | ((e & 7u) << 1));
+}
 
 // Shared-memory matrix descriptor: start address, leading / stride byte offsets,
 // descriptor version 1 (bits 46-47), base offset 0 (regions are 1024-aligned),
 // layout type in bits 61-63.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout = kLayoutSW128) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1u << 46;
-  d |= (uint64_t)kLayoutSW128 << 61;
+  d |= (uint64_t)(layout & 7u) << 61;
   return d;
 }
 

@@ -7,6 +7,8 @@
 //   mode 1 (P.V form):     out[128][n] = A[128 keys][128]^T . B[n][128 keys]^T
 //                          A by TMA read as an MN-major operand
 //   mode 2 / 3:            modes 0 / 1 with 64-wide rows (D = 64)
+//   mode 4:                mode 1 with B stored MN-major: rows = keys, n elements
+//                          per row under the 2n-byte swizzle (n = 16, 32, 64)
 #include "tc_common.cuh"
 
 namespace dropkv {
@@ -15,7 +17,7 @@ namespace {
 template <int D>
 __global__ void __launch_bounds__(128, 1)
     selftest_kernel(const __grid_constant__ CUtensorMap amap, const uint16_t* __restrict__ b, int n,
-                    int pv_form, float* __restrict__ out, int* __restrict__ status) {
+                    int pv_form, int mn_major, float* __restrict__ out, int* __restrict__ status) {
   extern __shared__ uint8_t raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   constexpr int A_BYTES = 128 * D * 2;
@@ -45,12 +47,18 @@ __global__ void __launch_bounds__(128, 1)
     for (int r = 0; r < D / 64; ++r)
       tc::tma_load_3d(As + r * 16384, &amap, &bars[0], 64 * r, 0, 0, tc::policy_evict_first());
   }
-  // B rows: K-major SW128, 64 elements per region row
+  // B rows: K-major SW128, 64 elements per region row (mn_major: rows = keys)
   const int bk = pv_form ? 128 : D;  // K extent of B
   for (int i = tid; i < n * bk; i += 128) {
     int row = i / bk, k = i % bk;
-    uint8_t* reg = Bs + (k / 64) * n * 128;
-    *reinterpret_cast<uint16_t*>(reg + tc::sw128_offset(row, k % 64)) = b[(size_t)row * bk + k];
+    if (mn_major) {
+      const uint32_t off = n == 16 ? tc::swz_offset<32>(k, row)
+                                   : (n == 32 ? tc::swz_offset<64>(k, row) : tc::swz_offset<128>(k, row));
+      *reinterpret_cast<uint16_t*>(Bs + off) = b[(size_t)row * bk + k];
+    } else {
+      uint8_t* reg = Bs + (k / 64) * n * 128;
+      *reinterpret_cast<uint16_t*>(reg + tc::sw128_offset(row, k % 64)) = b[(size_t)row * bk + k];
+    }
   }
   tc::fence_proxy_async_smem();
   __syncthreads();
@@ -68,12 +76,20 @@ __global__ void __launch_bounds__(128, 1)
           uint64_t bd = tc::smem_desc(b0 + (kk / 4) * n * 128 + (kk % 4) * 32, 16, 1024);
           tc::mma_f16(tmem, ad, bd, idesc, kk > 0);
         }
-      } else {
+      } else if (!mn_major) {
         const uint32_t idesc = tc::idesc_f16(true, 128, n, true, false);
         const uint32_t lbo = (D == 128) ? 16384 : 0;  // second 64-wide slab (D=64: repeat the first)
         for (int kk = 0; kk < 8; ++kk) {
           uint64_t ad = tc::smem_desc(a0 + kk * 2048, lbo, 1024);
           uint64_t bd = tc::smem_desc(b0 + (kk / 4) * n * 128 + (kk % 4) * 32, 16, 1024);
+          tc::mma_f16(tmem, ad, bd, idesc, kk > 0);
+        }
+      } else {
+        const uint32_t idesc = tc::idesc_f16(true, 128, n, true, true);
+        const uint32_t rb = 2 * n;  // bytes per key row of B
+        for (int kk = 0; kk < 8; ++kk) {
+          uint64_t ad = tc::smem_desc(a0 + kk * 2048, 16384, 1024);
+          uint64_t bd = tc::smem_desc(b0 + kk * 16 * rb, 0, 8 * rb, tc::layout_for_row_bytes(rb));
           tc::mma_f16(tmem, ad, bd, idesc, kk > 0);
         }
       }
@@ -110,11 +126,13 @@ using namespace dropkv;
 
 extern "C" int dropkv_selftest_tcgen05(int mode, const void* a, const void* b, int n, float* out,
                                        int* status, void* stream) {
-  if (mode < 0 || mode > 3) return fail(DROPKV_ERR_ARG, "selftest mode must be 0..3");
+  if (mode < 0 || mode > 4) return fail(DROPKV_ERR_ARG, "selftest mode must be 0..4");
   if (!(n == 16 || n == 32 || n == 64 || n == 128)) return fail(DROPKV_ERR_ARG, "n must be 16, 32, 64 or 128");
   if (!a || !b || !out || !status) return fail(DROPKV_ERR_ARG, "NULL pointer");
-  const int D = (mode >= 2) ? 64 : 128;
-  const int pv = mode & 1;
+  const int D = (mode == 2 || mode == 3) ? 64 : 128;
+  const int pv = (mode & 1) || mode == 4;
+  const int mn = mode == 4;
+  if (mn && n == 128) return fail(DROPKV_ERR_ARG, "mode 4 takes n = 16, 32 or 64");
   CUtensorMap map;
   int rc = make_kv_tensor_map(&map, a, 1, 128, D, true);
   if (rc) return rc;
@@ -124,10 +142,10 @@ extern "C" int dropkv_selftest_tcgen05(int mode, const void* a, const void* b, i
   const uint16_t* bb = reinterpret_cast<const uint16_t*>(b);
   if (D == 128) {
     cudaFuncSetAttribute(selftest_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    selftest_kernel<128><<<1, 128, smem, st>>>(map, bb, n, pv, out, status);
+    selftest_kernel<128><<<1, 128, smem, st>>>(map, bb, n, pv, mn, out, status);
   } else {
     cudaFuncSetAttribute(selftest_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    selftest_kernel<64><<<1, 128, smem, st>>>(map, bb, n, pv, out, status);
+    selftest_kernel<64><<<1, 128, smem, st>>>(map, bb, n, pv, mn, out, status);
   }
   return check_launch("selftest_tcgen05");
 }

@@ -13,10 +13,12 @@ from parity import assert_scores_close, well_conditioned
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("n", [16, 32, 64, 128])
 def test_tcgen05_selftest(mode, n):
-    D = 128 if mode < 2 else 64
+    if mode == 4 and n == 128:
+        pytest.skip("MN-major B rows hold at most 64 elements")
+    D = 64 if mode in (2, 3) else 128
     g = torch.Generator().manual_seed(mode * 1000 + n)
     A = torch.randn(128, D, generator=g).to(torch.bfloat16)
     kb = D if mode in (0, 2) else 128
