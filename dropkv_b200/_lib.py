@@ -28,6 +28,9 @@ SIGNATURES = {
     "dropkv_scores": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_int,
                                _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int, _c_p,
                                _c_p, _c_sz, _c_p]),
+    "dropkv_scores_static": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_int,
+                                      _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int,
+                                      _c_p, _c_p]),
     "dropkv_scorer_for": (_c_int, [_c_int] * 7),
     "dropkv_set_scorer": (_c_int, [_c_int]),
     "dropkv_scores_status_offset": (_c_sz, [_c_int] * 7),

@@ -4,6 +4,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -160,6 +161,31 @@ static int check_select_args(int B, int Hkv, int Lk, int kernel_size, int protec
   return DROPKV_OK;
 }
 
+// Scratch of dropkv_scores_static: a device array of this module, so the call
+// needs no allocation.  Its address is looked up once per device (with that device
+// current) and cached.
+static __device__ __align__(256) unsigned char g_static_scratch[DROPKV_STATIC_SCRATCH_BYTES];
+static std::mutex g_static_mu;
+static void* g_static_addr[64] = {nullptr};
+
+static int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(DROPKV_ERR_UNSUPPORTED, "device index %d is beyond 63", dev);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(DROPKV_ERR_CUDA, "cudaGetSymbolAddress of the static scratch on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    g_static_addr[dev] = p;
+  }
+  *out = g_static_addr[dev];
+  return DROPKV_OK;
+}
+
 }  // namespace dropkv
 
 using namespace dropkv;
@@ -210,6 +236,25 @@ int dropkv_scores(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64
   ScoreProblem p = make_problem(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, B, Hq, Hkv, Lk, D, window, eps,
                                 round_p, scores);
   return run_scores(p, dtype, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dropkv_scores_static(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                         const void* k, const void* v, int dtype, int B, int Hq, int Hkv, int Lk, int D,
+                         int window, float eps, int round_p, float* scores, void* stream) {
+  int rc = check_score_args(q, Lq, k, v, dtype, B, Hq, Hkv, Lk, D, window, round_p);
+  if (rc) return rc;
+  if (!scores) return fail(DROPKV_ERR_ARG, "scores must be a non-NULL device pointer");
+  const size_t need = scores_ws_bytes(dtype, B, Hkv, Lk, (Hq / Hkv) * window, D);
+  if (need > (size_t)DROPKV_STATIC_SCRATCH_BYTES)
+    return fail(DROPKV_ERR_WORKSPACE,
+                "dropkv_scores_static: this problem needs %zu bytes of scratch, more than the %zu-byte "
+                "static buffer; call dropkv_scores with a workspace instead",
+                need, (size_t)DROPKV_STATIC_SCRATCH_BYTES);
+  void* ws = nullptr;
+  if ((rc = static_scratch_address(&ws))) return rc;
+  ScoreProblem p = make_problem(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, B, Hq, Hkv, Lk, D, window, eps,
+                                round_p, scores);
+  return run_scores(p, dtype, ws, reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t dropkv_select_workspace_size(int B, int Hkv, int Lk) {

@@ -98,6 +98,37 @@ DROPKV_API int dropkv_set_scorer(int mode);
  * (size_t)-1 when the problem runs on the CUDA-core kernels. */
 DROPKV_API size_t dropkv_scores_status_offset(int dtype, int B, int Hq, int Hkv, int Lk, int D, int window);
 
+/* Size of the static device buffer dropkv_scores_static works in (16 MiB per
+ * device).  It covers one 128K-token Llama-3.1-8B layer (8 KV heads, 32 window
+ * rows, D = 128: about 10 MB of split partials on the tensor-core scorer). */
+#define DROPKV_STATIC_SCRATCH_BYTES (16u << 20)
+
+/* dropkv_scores without a workspace argument and without allocating anything:
+ * no cudaMalloc / cudaFree and no allocating library call.  For callers that may
+ * not allocate device memory when they score -- an engine that reserves all of
+ * its device memory up front in its own pool, or a host thread that must not
+ * enter an allocator -- and so cannot provide the scratch dropkv_scores takes.
+ * The scratch is a DROPKV_STATIC_SCRATCH_BYTES buffer compiled into the library
+ * (one per device).  Arguments, results and errors as dropkv_scores, plus:
+ *   - a problem whose scratch (dropkv_scores_workspace_size) exceeds the buffer
+ *     returns DROPKV_ERR_WORKSPACE with a message naming both sizes, and
+ *     launches nothing;
+ *   - the first call on each device looks the buffer's address up (and, like
+ *     every first scoring call, sets kernel attributes): make that first call
+ *     before any stream capture;
+ *   - the part of the scratch that must be zero when the kernels start (group
+ *     barrier counters, status word) is zeroed by the call itself on `stream`
+ *     (cudaMemsetAsync) before each launch; the caller initialises nothing;
+ *   - all calls on one device share the buffer: two calls whose work can overlap
+ *     on the device (unordered streams, or several host threads) race on it and
+ *     give wrong scores.  Order them (one stream, or events).
+ * No counterpart in the reference, whose scorer allocates its intermediates on
+ * every call (dropkv_triton.py:736-769). */
+DROPKV_API int dropkv_scores_static(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd,
+                                    int Lq, const void* k, const void* v, int dtype, int B, int Hq, int Hkv,
+                                    int Lk, int D, int window, float eps, int round_p, float* scores,
+                                    void* stream);
+
 /* Scratch bytes dropkv_select needs. */
 DROPKV_API size_t dropkv_select_workspace_size(int B, int Hkv, int Lk);
 
