@@ -25,7 +25,6 @@
  *   dropkv_select          <- dropkv_cache.py:462-477   max_pool1d + protect + topk + sort
  *   dropkv_gather          <- dropkv_cache.py:479-491   DropKVCache._gather_compressed
  *   dropkv_compress        <- dropkv_cache.py:355-491   _compute_keep_indices + _gather_compressed
- *   dropkv_compress_varlen <- dropkv_cache.py:355-491   the same, over a ragged list of heads
  */
 #ifndef DROPKV_B200_H
 #define DROPKV_B200_H
