@@ -80,9 +80,12 @@ struct __align__(16) SgShared {  // static part of the shared memory
   int sel[2];           // selected bin, remaining k
 };
 
+// RT: the pooling radius when known at compile time (unrolled block loops), or -1.
+template <int RT>
 __global__ void __launch_bounds__(SG_NT, 2) cluster_select_kernel(const float* __restrict__ scores, int Lk,
-                                                                  int chunk, int radius, int protect,
+                                                                  int chunk, int radius_rt, int protect,
                                                                   int keep_len, int64_t* __restrict__ keep_idx) {
+  const int radius = RT >= 0 ? RT : radius_rt;
   cg::cluster_group cluster = cg::this_cluster();
   const int CL = (int)cluster.num_blocks();
   const int r = (int)cluster.block_rank();
@@ -124,15 +127,34 @@ __global__ void __launch_bounds__(SG_NT, 2) cluster_select_kernel(const float* _
   const int wlen = 2 * radius + 1;
   for (int b = tid; b * wlen < H; b += SG_NT) {
     const int s0 = b * wlen, s1 = min(H, s0 + wlen);
-    float m = -INFINITY;
-    for (int x = s1 - 1; x >= s0; --x) {
-      m = fmaxf(m, buf[x]);
-      hsuf[x] = m;
-    }
-    m = -INFINITY;
-    for (int x = s0; x < s1; ++x) {
-      m = fmaxf(m, buf[x]);
-      buf[x] = m;
+    if (RT >= 0 && s1 - s0 == 2 * RT + 1) {  // whole block, unrolled: all loads issued together
+      constexpr int WL = 2 * (RT > 0 ? RT : 0) + 1;
+      float v[WL];
+#pragma unroll
+      for (int t = 0; t < WL; ++t) v[t] = buf[s0 + t];
+      float m = -INFINITY;
+#pragma unroll
+      for (int t = WL - 1; t >= 0; --t) {
+        m = fmaxf(m, v[t]);
+        hsuf[s0 + t] = m;
+      }
+      m = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < WL; ++t) {
+        m = fmaxf(m, v[t]);
+        buf[s0 + t] = m;
+      }
+    } else {
+      float m = -INFINITY;
+      for (int x = s1 - 1; x >= s0; --x) {
+        m = fmaxf(m, buf[x]);
+        hsuf[x] = m;
+      }
+      m = -INFINITY;
+      for (int x = s0; x < s1; ++x) {
+        m = fmaxf(m, buf[x]);
+        buf[x] = m;
+      }
     }
   }
   __syncthreads();
@@ -337,19 +359,21 @@ static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel
   size_t smem;
   const int cl = sg_cluster_for(Lk, kernel_size / 2, &chunk, &smem);
   if (!cl) return fail(DROPKV_ERR_UNSUPPORTED, "row of %d positions too long for the cluster select", Lk);
-  auto kern = cluster_select_kernel;
-  static unsigned long long attr_done = 0;  // per device: attributes set for the largest size used
-  static size_t attr_smem[64] = {0};
+  // the default kernel_size 11 gets the unrolled pooling
+  const bool r5 = kernel_size / 2 == 5;
+  auto kern = r5 ? cluster_select_kernel<5> : cluster_select_kernel<-1>;
+  static unsigned long long attr_done[2] = {0, 0};  // per variant and device: attributes set for
+  static size_t attr_smem[2][64] = {};              // the largest size used so far
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(attr_done & (1ull << dev)) || attr_smem[dev] < smem) {
+  if (dev >= 64 || !(attr_done[r5] & (1ull << dev)) || attr_smem[r5][dev] < smem) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %zu for the cluster select", smem);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       return fail(DROPKV_ERR_CUDA, "cannot allow 16-CTA clusters for the cluster select");
     if (dev < 64) {
-      attr_done |= (1ull << dev);
-      attr_smem[dev] = smem;
+      attr_done[r5] |= (1ull << dev);
+      attr_smem[r5][dev] = smem;
     }
   }
   cudaLaunchConfig_t cfg = {};
