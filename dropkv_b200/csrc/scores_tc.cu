@@ -130,7 +130,7 @@ struct Lay {
   static constexpr int RING = 0;
   static constexpr int QS = RING + NS * TILE;     // D/64 regions
   static constexpr int PS = QS + (D / 64) * RB;   // [NPB buffers][hi/lo] P tiles
-  static constexpr int YS = PS + NPB * 2 * PT;    // [hi/lo][D/64] regions
+  static constexpr int YS = PS + NPB * 2 * PT;    // [D/64][hi/lo] regions (hi and lo rows stacked)
   static constexpr int FL = YS + 2 * (D / 64) * RB;
   static constexpr int MLOC = FL;                 // floats [NPAD]
   static constexpr int LSE = MLOC + 4 * NPAD;
@@ -191,9 +191,16 @@ __device__ __forceinline__ float2 unpack2<__half>(uint32_t u) {
   return __half22float2(*reinterpret_cast<__half2*>(&u));
 }
 
+// p rounded to the input dtype (p in [0, 1], finite).  bf16 round-to-nearest-even
+// is done on the integer pipe: add 0x7fff plus the lowest kept bit, clear the 16
+// dropped bits (exact for finite non-negative inputs); this keeps the conversion
+// unit, which also serves exp2 and the reciprocal, free.
 template <int ROUND>
 __device__ __forceinline__ float round_p_t(float p) {
-  if (ROUND == DROPKV_ROUND_BF16) return __bfloat162float(__float2bfloat16_rn(p));
+  if (ROUND == DROPKV_ROUND_BF16) {
+    const uint32_t u = __float_as_uint(p);
+    return __uint_as_float((u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u);
+  }
   if (ROUND == DROPKV_ROUND_F16) return __half2float(__float2half_rn(p));
   return p;
 }
@@ -272,7 +279,7 @@ __global__ void __launch_bounds__(NTH, 1)
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int NREG = D / 64;            // 64-wide slabs of a K/V/Q/Y row
   constexpr int TMAX = L::TMAX;
-  constexpr int S2COL = TMAX * NPAD;      // y^T accumulator / S2 buffer 0; buffer 1 follows
+  constexpr int S2COL = TMAX * NPAD;      // y^T accumulator / S2: 2*NPAD columns (hi part, lo part)
   constexpr int HC = NPAD / 4;            // query columns per epilogue warp
   constexpr int PRB = L::PRB;
   constexpr int EPC = D / 4;              // V-row elements per column group (||v||^2)
@@ -389,7 +396,9 @@ __global__ void __launch_bounds__(NTH, 1)
       const uint32_t ps0 = tc::smem_addr(sm + L::PS);
       const uint32_t ys0 = tc::smem_addr(sm + L::YS);
       constexpr uint32_t ID_QK = tc::idesc_f16(BF16, 128, NPAD, false, false);
-      constexpr uint32_t ID_PV = tc::idesc_f16(BF16, 128, NPAD, true, true);
+      // hi and lo halves stacked along N: one MMA per k-step reads the V tile once
+      constexpr uint32_t ID_PV = tc::idesc_f16(BF16, 128, 2 * NPAD, true, true);
+      constexpr uint32_t ID_S2 = tc::idesc_f16(BF16, 128, 2 * NPAD, false, false);
       constexpr uint32_t LBO_PV = (NREG == 2) ? 16384u : 0u;
       constexpr uint32_t LAYOUT_P = tc::layout_for_row_bytes(PRB);
       uint32_t k = 0;  // ring position
@@ -423,14 +432,12 @@ __global__ void __launch_bounds__(NTH, 1)
           tc::tc_fence_after();
           const uint32_t a0 = ring0 + slot * L::TILE;
           const uint32_t pb = ps0 + buf * 2 * L::PT;
+          // B: the P_hi tile and, one leading-byte-offset (a tile) further, P_lo
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t ad = tc::smem_desc(a0 + kk * 2048, LBO_PV, 1024);
-              const uint64_t bd = tc::smem_desc(pb + half * L::PT + kk * 16 * PRB, 0, 8 * PRB, LAYOUT_P);
-              tc::mma_f16(tmem + S2COL, ad, bd, ID_PV, (i > 0 || half > 0 || kk > 0) ? 1u : 0u);
-            }
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = tc::smem_desc(a0 + kk * 2048, LBO_PV, 1024);
+            const uint64_t bd = tc::smem_desc(pb + kk * 16 * PRB, L::PT, 8 * PRB, LAYOUT_P);
+            tc::mma_f16(tmem + S2COL, ad, bd, ID_PV, (i > 0 || kk > 0) ? 1u : 0u);
           }
           tc::mma_commit(&freeb[slot]);
           tc::mbar_arrive_cnt(&freeb[slot], NEW);
@@ -442,31 +449,27 @@ __global__ void __launch_bounds__(NTH, 1)
         tc::tc_fence_after();
         for (int i = 0; i < nt; ++i, ++k) {
           const uint32_t slot = k % NS;
-          const int buf = i & 1;
           if (!wait_bar(&full[slot], (k / NS) & 1, 25)) break;
-          if (i >= 2) {
-            if (!wait_bar(&bx[B_S2FREE0 + buf], c_s2free[buf] & 1, 26)) break;
-            ++c_s2free[buf];
+          if (i >= 1) {  // the epilogue has read S2 of tile i - 1
+            if (!wait_bar(&bx[B_S2FREE0], c_s2free[0] & 1, 26)) break;
+            ++c_s2free[0];
           }
           tc::tc_fence_after();
           const uint32_t a0 = ring0 + slot * L::TILE;
+          // B: y_hi rows then y_lo rows of each 64-wide slab (N = 2 * NPAD)
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint64_t ad = tc::smem_desc(a0 + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024);
-              const uint64_t bd = tc::smem_desc(ys0 + half * NREG * L::RB + (kk / 4) * L::RB + (kk % 4) * 32, 16, 1024);
-              tc::mma_f16(tmem + S2COL + buf * NPAD, ad, bd, ID_QK, (half > 0 || kk > 0) ? 1u : 0u);
-            }
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t ad = tc::smem_desc(a0 + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024);
+            const uint64_t bd = tc::smem_desc(ys0 + (kk / 4) * 2 * L::RB + (kk % 4) * 32, 16, 1024);
+            tc::mma_f16(tmem + S2COL, ad, bd, ID_S2, kk > 0 ? 1u : 0u);
           }
           tc::mma_commit(&freeb[slot]);  // the epilogue warps add theirs after ||v||^2
-          tc::mma_commit(&bx[B_S2READY0 + buf]);
+          tc::mma_commit(&bx[B_S2READY0]);
         }
-        // the last (up to two) S2 buffers are released after this round's epilogue
-        for (int i = (nt >= 2 ? nt - 2 : 0); i < nt; ++i) {
-          const int buf = i & 1;
-          if (!wait_bar(&bx[B_S2FREE0 + buf], c_s2free[buf] & 1, 27)) break;
-          ++c_s2free[buf];
+        // the last S2 is released after this round's epilogue
+        if (nt > 0) {
+          if (!wait_bar(&bx[B_S2FREE0], c_s2free[0] & 1, 27)) break;
+          ++c_s2free[0];
         }
       }
       tc::mma_commit(&bx[B_FIN]);
@@ -608,11 +611,14 @@ __global__ void __launch_bounds__(NTH, 1)
         const float inv = 1.0f / a.pscale;
         const int d = q * 32 + lane;  // TMEM lane of the y^T accumulator = d
         if (d < D) {
-          float v[HC];
-          if (nt > 0) tmem_ld<HC>(tmem + lrow + S2COL + cbase, v);
+          float v[HC], vl[HC];
+          if (nt > 0) {
+            tmem_ld<HC>(tmem + lrow + S2COL + cbase, v);
+            tmem_ld<HC>(tmem + lrow + S2COL + NPAD + cbase, vl);
+          }
 #pragma unroll
           for (int j = 0; j < HC; ++j)
-            if (colok[j]) __stcg(a.part_y + (prow + cbase + j) * D + d, nt > 0 ? v[j] * inv : 0.f);
+            if (colok[j]) __stcg(a.part_y + (prow + cbase + j) * D + d, nt > 0 ? (v[j] + vl[j]) * inv : 0.f);
         }
       }
       tc::tc_fence_before();
@@ -775,9 +781,9 @@ __global__ void __launch_bounds__(NTH, 1)
               const float2 back = unpack2<T>(hw[k2 / 2]);
               lw[k2 / 2] = pack2<T>(y[k2] - back.x, y[k2 + 1] - back.y);
             }
-            const uint32_t off = (d / 64) * L::RB + m * 128 + ((((d % 64) >> 3) ^ (m & 7)) << 4);
+            const uint32_t off = (d / 64) * 2 * L::RB + m * 128 + ((((d % 64) >> 3) ^ (m & 7)) << 4);
             *reinterpret_cast<uint4*>(sm + L::YS + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4*>(sm + L::YS + NREG * L::RB + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            *reinterpret_cast<uint4*>(sm + L::YS + L::RB + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
           }
         }
 #pragma unroll
@@ -802,18 +808,21 @@ __global__ void __launch_bounds__(NTH, 1)
       }
       const int vslab = (cg * EPC) / 64, vc0 = ((cg * EPC) % 64) / 8;
       for (int i = 0; i < nt; ++i) {
-        const int buf = i & 1;
+        const int buf = i & 1;  // exchange buffer
         const uint32_t kpos = (uint32_t)rd * 3u * nt + 2u * nt + i;  // ring position of V tile i
         const uint32_t slot = kpos % NS;
-        wait_bar(&bx[B_S2READY0 + buf], c_s2r[buf] & 1, 36);
-        ++c_s2r[buf];
+        wait_bar(&bx[B_S2READY0], c_s2r[0] & 1, 36);
+        ++c_s2r[0];
         tc::tc_fence_after();
-        float s[HC], s2[HC];
+        float s[HC], s2[HC], s2l[HC];
         tmem_ld<HC>(tmem + lrow + i * NPAD + cbase, s);
-        tmem_ld<HC>(tmem + lrow + S2COL + buf * NPAD + cbase, s2);
+        tmem_ld<HC>(tmem + lrow + S2COL + cbase, s2);
+        tmem_ld<HC>(tmem + lrow + S2COL + NPAD + cbase, s2l);
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&bx[B_S2FREE0 + buf]);
+        if (lane == 0) tc::mbar_arrive(&bx[B_S2FREE0]);
+#pragma unroll
+        for (int j = 0; j < HC; ++j) s2[j] += s2l[j];
         // ||v_j||^2 over this group's EPC elements of the row; the slot is held for
         // this read by the arrival below (its full phase has completed: the S2 MMA
         // read the tile)

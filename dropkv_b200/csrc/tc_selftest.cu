@@ -9,6 +9,9 @@
 //   mode 2 / 3:            modes 0 / 1 with 64-wide rows (D = 64)
 //   mode 4:                mode 1 with B stored MN-major: rows = keys, n elements
 //                          per row under the 2n-byte swizzle (n = 16, 32, 64)
+//   mode 5:                mode 4 with N = n split into two swizzle atoms of n/2
+//                          columns, the second atom 128 rows further (LBO)
+//                          (n = 32, 64, 128)
 #include "tc_common.cuh"
 
 namespace dropkv {
@@ -51,7 +54,13 @@ __global__ void __launch_bounds__(128, 1)
   const int bk = pv_form ? 128 : D;  // K extent of B
   for (int i = tid; i < n * bk; i += 128) {
     int row = i / bk, k = i % bk;
-    if (mn_major) {
+    if (mn_major == 2) {  // two atoms of n/2 columns, the second at 128 rows x n bytes
+      const int at = n / 2, t = row / at, c = row % at;
+      const uint32_t off = (uint32_t)t * 128u * (uint32_t)n +
+                           (at == 16 ? tc::swz_offset<32>(k, c)
+                                     : (at == 32 ? tc::swz_offset<64>(k, c) : tc::swz_offset<128>(k, c)));
+      *reinterpret_cast<uint16_t*>(Bs + off) = b[(size_t)row * bk + k];
+    } else if (mn_major) {
       const uint32_t off = n == 16 ? tc::swz_offset<32>(k, row)
                                    : (n == 32 ? tc::swz_offset<64>(k, row) : tc::swz_offset<128>(k, row));
       *reinterpret_cast<uint16_t*>(Bs + off) = b[(size_t)row * bk + k];
@@ -82,6 +91,14 @@ __global__ void __launch_bounds__(128, 1)
         for (int kk = 0; kk < 8; ++kk) {
           uint64_t ad = tc::smem_desc(a0 + kk * 2048, lbo, 1024);
           uint64_t bd = tc::smem_desc(b0 + (kk / 4) * n * 128 + (kk % 4) * 32, 16, 1024);
+          tc::mma_f16(tmem, ad, bd, idesc, kk > 0);
+        }
+      } else if (mn_major == 2) {
+        const uint32_t idesc = tc::idesc_f16(true, 128, n, true, true);
+        const uint32_t rb = n;  // bytes per key row of one atom (n/2 columns)
+        for (int kk = 0; kk < 8; ++kk) {
+          uint64_t ad = tc::smem_desc(a0 + kk * 2048, 16384, 1024);
+          uint64_t bd = tc::smem_desc(b0 + kk * 16 * rb, 128 * rb, 8 * rb, tc::layout_for_row_bytes(rb));
           tc::mma_f16(tmem, ad, bd, idesc, kk > 0);
         }
       } else {
@@ -126,13 +143,14 @@ using namespace dropkv;
 
 extern "C" int dropkv_selftest_tcgen05(int mode, const void* a, const void* b, int n, float* out,
                                        int* status, void* stream) {
-  if (mode < 0 || mode > 4) return fail(DROPKV_ERR_ARG, "selftest mode must be 0..4");
+  if (mode < 0 || mode > 5) return fail(DROPKV_ERR_ARG, "selftest mode must be 0..5");
   if (!(n == 16 || n == 32 || n == 64 || n == 128)) return fail(DROPKV_ERR_ARG, "n must be 16, 32, 64 or 128");
   if (!a || !b || !out || !status) return fail(DROPKV_ERR_ARG, "NULL pointer");
   const int D = (mode == 2 || mode == 3) ? 64 : 128;
-  const int pv = (mode & 1) || mode == 4;
-  const int mn = mode == 4;
-  if (mn && n == 128) return fail(DROPKV_ERR_ARG, "mode 4 takes n = 16, 32 or 64");
+  const int pv = (mode & 1) || mode >= 4;
+  const int mn = mode == 4 ? 1 : (mode == 5 ? 2 : 0);
+  if (mode == 4 && n == 128) return fail(DROPKV_ERR_ARG, "mode 4 takes n = 16, 32 or 64");
+  if (mode == 5 && n == 16) return fail(DROPKV_ERR_ARG, "mode 5 takes n = 32, 64 or 128");
   CUtensorMap map;
   int rc = make_kv_tensor_map(&map, a, 1, 128, D, true);
   if (rc) return rc;

@@ -160,7 +160,8 @@ DROPKV_API int dropkv_compress(const void* q, int64_t q_sb, int64_t q_sh, int64_
 /* Diagnostic: one 128-row tile through a tcgen05 MMA form used by the fused
  * scorer (mode 0: out[128][n] = A[128][128] B[n][128]^T with A loaded by TMA;
  * mode 1: out[128][n] = A[128][128]^T B[n][128]^T with A read MN-major; modes 2/3:
- * the same with 64-wide A rows; mode 4: mode 1 with B stored MN-major, n = 16/32/64).  a, b bf16 row-major; out fp32 [128][n];
+ * the same with 64-wide A rows; mode 4: mode 1 with B stored MN-major, n = 16/32/64;
+ * mode 5: mode 4 with B split into two MN-major atoms of n/2 columns, n = 32/64/128).  a, b bf16 row-major; out fp32 [128][n];
  * *status (device int, zeroed by the caller) becomes non-zero if a wait timed out.
  * No counterpart in the reference: a hardware check of this library's building
  * blocks. */
