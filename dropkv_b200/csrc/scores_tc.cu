@@ -89,6 +89,7 @@ constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
 constexpr int kMaxGs = 256;                  // CTAs per head group (at most)
 constexpr int kWts = 1024;                   // merge maxima / sums buffers (floats each)
 constexpr int kMaxTiles = 30;                // TMEM logit tiles per CTA and head (N = 16)
+constexpr int kVnWarps = 4;                  // epilogue warps that read a pass-1 V tile for ||v||^2
 
 struct TcArgs {
   ScoreProblem p;
@@ -137,8 +138,9 @@ struct Lay {
   static constexpr int YN = LSE + 4 * NPAD;
   static constexpr int BND = YN + 4 * NPAD;       // int [NPAD] causal bound per row
   static constexpr int RED = BND + 4 * NPAD;      // [4 lane quadrants][NPAD]
-  static constexpr int XCH = RED + 16 * NPAD;     // [2 buf][3 column groups][4 sums][TK]
-  static constexpr int WTS = XCH + 4 * 24 * TK;   // [2][kWts]
+  static constexpr int XCH = RED + 16 * NPAD;     // [2 buf][3 column groups][3 sums][TK]
+  static constexpr int VN = XCH + 4 * 18 * TK;    // [TMAX][TK] ||v||^2 of the CTA's keys
+  static constexpr int WTS = VN + 4 * TMAX * TK;  // [2][kWts]
   static constexpr int BAR = WTS + 8 * kWts;      // mbarriers
   static constexpr int NBAR = 2 * NS + kMaxTiles + kAuxBars;
   static constexpr int MISC = BAR + 8 * NBAR;     // tmem slot, flags
@@ -195,6 +197,14 @@ __device__ __forceinline__ float2 unpack2<__half>(uint32_t u) {
 // is done on the integer pipe: add 0x7fff plus the lowest kept bit, clear the 16
 // dropped bits (exact for finite non-negative inputs); this keeps the conversion
 // unit, which also serves exp2 and the reciprocal, free.
+// 2^x by the hardware approximation (relative error ~2^-22; results below 2^-126
+// flush to zero, far below any weight that reaches a score).
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <int ROUND>
 __device__ __forceinline__ float round_p_t(float p) {
   if (ROUND == DROPKV_ROUND_BF16) {
@@ -282,7 +292,6 @@ __global__ void __launch_bounds__(NTH, 1)
   constexpr int S2COL = TMAX * NPAD;      // y^T accumulator / S2: 2*NPAD columns (hi part, lo part)
   constexpr int HC = NPAD / 4;            // query columns per epilogue warp
   constexpr int PRB = L::PRB;
-  constexpr int EPC = D / 4;              // V-row elements per column group (||v||^2)
   static_assert(TMAX <= kMaxTiles, "s_done barriers");
   static_assert(HC >= 4 && HC <= 16, "column split");
   extern __shared__ uint8_t raw[];
@@ -300,6 +309,7 @@ __global__ void __launch_bounds__(NTH, 1)
   float* red = reinterpret_cast<float*>(sm + L::RED);
   float* xch = reinterpret_cast<float*>(sm + L::XCH);
   float* wts = reinterpret_cast<float*>(sm + L::WTS);
+  float* vn_s = reinterpret_cast<float*>(sm + L::VN);
   float* sts = wts + kWts;
 
   const ScoreProblem& p = a.p;
@@ -312,10 +322,10 @@ __global__ void __launch_bounds__(NTH, 1)
 
   if (tid == 0) {
     for (int i = 0; i < L::NBAR; ++i) tc::mbar_init(&full[i], 1);
-    // a ring slot is free after its MMA (commit) and one arrival per epilogue warp;
-    // for K and pass-1 V tiles, which the epilogue never reads, the MMA thread
-    // makes those arrivals itself
-    for (int s = 0; s < NS; ++s) tc::mbar_init(&freeb[s], 1 + NEW);
+    // a ring slot is free after its MMA (commit) and kVnWarps arrivals: by the
+    // epilogue warps that read a pass-1 V tile for ||v||^2, by the MMA thread
+    // itself for K tiles and pass-2 V tiles
+    for (int s = 0; s < NS; ++s) tc::mbar_init(&freeb[s], 1 + kVnWarps);
     tc::mbar_init(&bx[B_PREADY0], NEW);
     tc::mbar_init(&bx[B_PREADY1], NEW);
     tc::mbar_init(&bx[B_S2FREE0], NEW);
@@ -419,7 +429,7 @@ __global__ void __launch_bounds__(NTH, 1)
             tc::mma_f16(tmem + i * NPAD, ad, bd, ID_QK, kk > 0);
           }
           tc::mma_commit(&freeb[slot]);
-          tc::mbar_arrive_cnt(&freeb[slot], NEW);
+          tc::mbar_arrive_cnt(&freeb[slot], kVnWarps);
           tc::mma_commit(&sdone[i]);
         }
         // pass 1c: y^T += V_i^T (p_hi + p_lo)^T
@@ -439,8 +449,7 @@ __global__ void __launch_bounds__(NTH, 1)
             const uint64_t bd = tc::smem_desc(pb + kk * 16 * PRB, L::PT, 8 * PRB, LAYOUT_P);
             tc::mma_f16(tmem + S2COL, ad, bd, ID_PV, (i > 0 || kk > 0) ? 1u : 0u);
           }
-          tc::mma_commit(&freeb[slot]);
-          tc::mbar_arrive_cnt(&freeb[slot], NEW);
+          tc::mma_commit(&freeb[slot]);  // + the ||v||^2 warps' arrivals
           tc::mma_commit(&bx[B_PFREE0 + buf]);
         }
         tc::mma_commit(&bx[B_YDONE]);
@@ -463,7 +472,8 @@ __global__ void __launch_bounds__(NTH, 1)
             const uint64_t bd = tc::smem_desc(ys0 + (kk / 4) * 2 * L::RB + (kk % 4) * 32, 16, 1024);
             tc::mma_f16(tmem + S2COL, ad, bd, ID_S2, kk > 0 ? 1u : 0u);
           }
-          tc::mma_commit(&freeb[slot]);  // the epilogue warps add theirs after ||v||^2
+          tc::mma_commit(&freeb[slot]);
+          tc::mbar_arrive_cnt(&freeb[slot], kVnWarps);
           tc::mma_commit(&bx[B_S2READY0]);
         }
         // the last S2 is released after this round's epilogue
@@ -573,7 +583,7 @@ __global__ void __launch_bounds__(NTH, 1)
 #pragma unroll
         for (int j = 0; j < HC; ++j) {
           const bool ok = (edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j]) && ml[j] != -INFINITY;
-          const float pr = ok ? exp2f(fmaf(s[j], a.c, -ml[j])) : 0.f;
+          const float pr = ok ? ex2f(fmaf(s[j], a.c, -ml[j])) : 0.f;
           ssum[j] += pr;
           ps[j] = pr * a.pscale;
         }
@@ -583,6 +593,33 @@ __global__ void __launch_bounds__(NTH, 1)
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bx[B_PREADY0 + buf]);
+        // ||v_j||^2 of V tile i, by column group i % 4; the tile's ring slot waits
+        // for these four warps.  Its full phase is unambiguous: the slot's previous
+        // load was consumed before this round's logits (K) or P.V (tile i - NS).
+        if (cg == (i & 3)) {
+          const uint32_t kpos = (uint32_t)rd * 3u * nt + (uint32_t)nt + (uint32_t)i;  // ring position
+          const uint32_t slot = kpos % NS;
+          wait_bar(&full[slot], (kpos / NS) & 1, 32);
+          float vn = 0.f;
+#pragma unroll
+          for (int rr = 0; rr < NREG; ++rr) {
+            const uint8_t* vt = sm + L::RING + slot * L::TILE + rr * 16384 + jkey * 128;
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8) {
+              const uint4 r4 = *reinterpret_cast<const uint4*>(vt + ((c8 ^ (jkey & 7)) << 4));
+              const uint32_t w4[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+              for (int k2 = 0; k2 < 4; ++k2) {
+                const float2 x = unpack2<T>(w4[k2]);
+                vn = fmaf(x.x, x.x, vn);
+                vn = fmaf(x.y, x.y, vn);
+              }
+            }
+          }
+          vn_s[i * TK + jkey] = vn;
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&freeb[slot]);
+        }
       }
       // y^T complete
       if (nt > 0) wait_bar(&bx[B_YDONE], rd & 1, 33);
@@ -799,18 +836,15 @@ __global__ void __launch_bounds__(NTH, 1)
       if (et == 0) tc::mbar_arrive(&bx[B_YREADY]);
       stamp(rd, TR_YSTAGE);
 
-      // ---- pass 2: score epilogue over S (TMEM, pass 1), S2 = <v, y> and ||v||^2 ----
+      // ---- pass 2: score epilogue over S (TMEM, pass 1), S2 = <v, y> and ||v||^2 (pass 1c) ----
       float lsel[HC], ynl[HC];
 #pragma unroll
       for (int j = 0; j < HC; ++j) {
         lsel[j] = lse_s[cbase + j];
         ynl[j] = yn_s[cbase + j];
       }
-      const int vslab = (cg * EPC) / 64, vc0 = ((cg * EPC) % 64) / 8;
       for (int i = 0; i < nt; ++i) {
         const int buf = i & 1;  // exchange buffer
-        const uint32_t kpos = (uint32_t)rd * 3u * nt + 2u * nt + i;  // ring position of V tile i
-        const uint32_t slot = kpos % NS;
         wait_bar(&bx[B_S2READY0], c_s2r[0] & 1, 36);
         ++c_s2r[0];
         tc::tc_fence_after();
@@ -823,34 +857,13 @@ __global__ void __launch_bounds__(NTH, 1)
         if (lane == 0) tc::mbar_arrive(&bx[B_S2FREE0]);
 #pragma unroll
         for (int j = 0; j < HC; ++j) s2[j] += s2l[j];
-        // ||v_j||^2 over this group's EPC elements of the row; the slot is held for
-        // this read by the arrival below (its full phase has completed: the S2 MMA
-        // read the tile)
-        wait_bar(&full[slot], (kpos / NS) & 1, 32);
-        float vn = 0.f;
-        {
-          const uint8_t* vt = sm + L::RING + slot * L::TILE + vslab * 16384 + jkey * 128;
-#pragma unroll
-          for (int c8 = 0; c8 < EPC / 8; ++c8) {
-            const uint4 r4 = *reinterpret_cast<const uint4*>(vt + (((vc0 + c8) ^ (jkey & 7)) << 4));
-            const uint32_t w4[4] = {r4.x, r4.y, r4.z, r4.w};
-#pragma unroll
-            for (int k2 = 0; k2 < 4; ++k2) {
-              const float2 x = unpack2<T>(w4[k2]);
-              vn = fmaf(x.x, x.x, vn);
-              vn = fmaf(x.y, x.y, vn);
-            }
-          }
-        }
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&freeb[slot]);
         const int key = (t0 + i) * TK + jkey;
         const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
         float sw = 0.f, sb = 0.f, sc = 0.f;
 #pragma unroll
         for (int j = 0; j < HC; ++j) {
           const bool ok = edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j];
-          float pr = exp2f(fmaf(s[j], a.c, -lsel[j]));
+          float pr = ex2f(fmaf(s[j], a.c, -lsel[j]));
           pr = fminf(pr, 1.f);
           pr = round_p_t<ROUND>(pr);
           const float ratio = __fdividef(pr, 1.f - pr + p.eps);
@@ -860,24 +873,23 @@ __global__ void __launch_bounds__(NTH, 1)
           sc = fmaf(w, ynl[j], sc);
         }
         // column groups 1-3 hand their sums to group 0 (fixed order: deterministic)
-        float* xb = xch + buf * 12 * TK;
+        float* xb = xch + buf * 9 * TK;
         if (cg > 0) {
-          float* xg = xb + (cg - 1) * 4 * TK;
+          float* xg = xb + (cg - 1) * 3 * TK;
           xg[jkey] = sw;
           xg[TK + jkey] = sb;
           xg[2 * TK + jkey] = sc;
-          xg[3 * TK + jkey] = vn;
         }
         quad_sync(q);
         if (cg == 0 && key < Lk) {
 #pragma unroll
           for (int g3 = 0; g3 < 3; ++g3) {
-            const float* xg = xb + g3 * 4 * TK;
+            const float* xg = xb + g3 * 3 * TK;
             sw += xg[jkey];
             sb += xg[TK + jkey];
             sc += xg[2 * TK + jkey];
-            vn += xg[3 * TK + jkey];
           }
+          const float vn = vn_s[i * TK + jkey];
           p.scores[(size_t)h * Lk + key] = (sw * vn - 2.f * sb + sc) / (float)p.g;
         }
       }
