@@ -77,6 +77,27 @@ int make_kv_tensor_map(CUtensorMap* map, const void* base, int BH, int L, int D,
   return DROPKV_OK;
 }
 
+// Q viewed as {D, Lq, Hq, B} with box {64, W, g, 1}: one load per 64-wide slab
+// brings the W window rows of the g query heads of one KV head, in the order of
+// the scorer's query rows (m = head * W + row), under the 128-byte swizzle.
+// Only for Q with unit element stride and 16-byte aligned base and strides;
+// returns false (and encodes nothing) otherwise.
+bool make_q_tensor_map(CUtensorMap* map, const ScoreProblem& p, bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || p.q_sd != 1 || (p.D % 64) || p.W > 256 || p.g > 256) return false;
+  const int64_t sb[3] = {p.q_ss * 2, p.q_sh * 2, p.q_sb * 2};
+  if (reinterpret_cast<uintptr_t>(p.q) % 16) return false;
+  for (int i = 0; i < 3; ++i)
+    if (sb[i] <= 0 || sb[i] % 16 || sb[i] >= (int64_t(1) << 40)) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)p.D, (cuuint64_t)p.Lq, (cuuint64_t)p.Hq, (cuuint64_t)p.B};
+  cuuint64_t strides[3] = {(cuuint64_t)sb[0], (cuuint64_t)sb[1], (cuuint64_t)sb[2]};
+  cuuint32_t box[4] = {64, (cuuint32_t)p.W, (cuuint32_t)p.g, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                  const_cast<void*>(p.q), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
 
 namespace {
 
@@ -104,6 +125,7 @@ struct TcArgs {
   float* y_g;    // [BH][M][D]
   float* lse_g;  // [BH][M]      (base-2)
   int* status;   // device status word (0 = ok)
+  int q_tma;     // 1: the TMA warp loads the Q window (qmap), 0: the epilogue stages it
   unsigned long long* trace;  // per CTA and round: globaltimer at phase ends
 };
 
@@ -284,7 +306,7 @@ __device__ __forceinline__ void store_p(uint8_t* hi_tile, uint8_t* lo_tile, int 
 template <typename T, int D, int NPAD, int NS, int NPB, int ROUND>
 __global__ void __launch_bounds__(NTH, 1)
     fused_scores_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                        TcArgs a) {
+                        const __grid_constant__ CUtensorMap qmap, TcArgs a) {
   using L = Lay<D, NPAD, NS, NPB>;
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int NREG = D / 64;            // 64-wide slabs of a K/V/Q/Y row
@@ -345,6 +367,13 @@ __global__ void __launch_bounds__(NTH, 1)
   if (tid < NPAD) {
     bnd_s[tid] = (tid < M) ? (Lk - W + tid % W) : -1;
   }
+  if (a.q_tma) {  // query rows M .. NPAD-1 of the Q operand stay zero (TMA writes rows < M)
+    for (int i = tid; i < (NPAD - M) * D; i += NTH) {
+      const int m = M + i / D, d = i % D;
+      *reinterpret_cast<uint16_t*>(sm + L::QS + (d / 64) * L::RB + tc::sw128_offset(m, d % 64)) = 0;
+    }
+    tc::fence_proxy_async_smem();
+  }
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -379,10 +408,29 @@ __global__ void __launch_bounds__(NTH, 1)
       const uint64_t pol_last = tc::policy_evict_last();
       tc::tma_prefetch_desc(&kmap);
       tc::tma_prefetch_desc(&vmap);
+      // Q window of round r into the Q operand; QREADY's phase r completes on arrival
+      auto load_q = [&](int r) {
+        const int h = r * a.groups + grp;
+        const int b = h / p.Hkv, hkv = h % p.Hkv;
+        tc::mbar_arrive_expect_tx(&bx[B_QREADY], (uint32_t)(128 * M * NREG));
+        for (int rr = 0; rr < NREG; ++rr)
+          tc::tma_load_4d(sm + L::QS + rr * L::RB, &qmap, &bx[B_QREADY], 64 * rr, p.Lq - W, hkv * p.g, b);
+      };
+      if (a.q_tma) {
+        tc::tma_prefetch_desc(&qmap);
+        if (my_rounds > 0) load_q(0);
+      }
       const uint32_t total = (uint32_t)my_rounds * 3u * (uint32_t)nt;
       uint32_t k = 0;
       for (; k < total; ++k) {
         const uint32_t slot = k % NS;
+        if (a.q_tma && k % (3u * nt) == 2u * nt && (int)(k / (3u * nt)) + 1 < my_rounds) {
+          // before this round's pass-2 loads: the round's logits are done with the
+          // Q operand (its last logit tile has completed), so the next Q can come
+          const int r = (int)(k / (3u * nt));
+          if (!wait_bar(&sdone[nt - 1], r & 1, 5)) break;
+          load_q(r + 1);
+        }
         if (k >= NS && !wait_bar(&freeb[slot], ((k / NS) - 1) & 1, 2)) break;
         const int r = (int)(k / (3u * nt));
         const int stage = (int)((k / nt) % 3u);
@@ -508,8 +556,8 @@ __global__ void __launch_bounds__(NTH, 1)
       const int b = h / p.Hkv, hkv = h % p.Hkv;
       stamp(rd, TR_START);
 
-      // ---- Q window -> SW128 K-major operand ----------------------------------
-      {
+      // ---- Q window -> SW128 K-major operand (unless the TMA warp loads it) ------
+      if (!a.q_tma) {
         const T* qp = reinterpret_cast<const T*>(p.q);
 #pragma unroll 4
         for (int i = et; i < NPAD * D; i += NEPI) {
@@ -969,6 +1017,9 @@ static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cuda
   if (rc) return rc;
   rc = make_kv_tensor_map(&vm, p.v, BH, p.Lk, D, bf16);
   if (rc) return rc;
+  CUtensorMap qm;
+  std::memset(&qm, 0, sizeof(qm));
+  const bool q_tma = make_q_tensor_map(&qm, p, bf16);
   char* base = reinterpret_cast<char*>(ws);
   TcArgs a;
   a.p = p;
@@ -976,6 +1027,7 @@ static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cuda
   a.gs = t.gs; a.groups = t.groups; a.rounds = t.rounds; a.tiles = t.tiles; a.tmax = t.tmax;
   a.c = (float)(1.4426950408889634 / std::sqrt((double)p.D));
   a.pscale = bf16 ? 1.0f : 32768.0f;
+  a.q_tma = q_tma ? 1 : 0;
   a.ctr = reinterpret_cast<int*>(base + t.off_ctr);
   a.status = reinterpret_cast<int*>(base + t.off_status);
   a.trace = reinterpret_cast<unsigned long long*>(base + t.off_trace);
@@ -1005,7 +1057,7 @@ static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cuda
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, km, vm, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, km, vm, qm, a);
   if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "fused scorer launch: %s", cudaGetErrorString(e));
   return check_launch("fused_scores", 2);
 }

@@ -96,6 +96,28 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, uint64_t
       : "memory");
 }
 
+// 4-D tile load {c0 (innermost), c1, c2, c3} into shared memory, completion on `bar`.
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* map, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// 3-D tile prefetch into L2 only: no shared memory, no completion signal.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* map, int c0, int c1, int c2, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile.L2::cache_hint [%0, {%1, %2, %3}], %4;" ::"l"(map),
+               "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+               : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 // Generic-proxy shared-memory writes -> visible to the async proxy (MMA / TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
