@@ -15,6 +15,13 @@ Multi-GPU (torchrun, one rank per GPU): every rank processes its own layer
 (weak scaling, no collective on the data path); value = all ranks' positions /
 max over ranks of the device-timed region.
 
+``--workload ragged``: the config-5 batch (16 sequences, Lk drawn uniformly
+from [4096, 65536], 32 Llama layers each), split across ranks by
+(sequence, layer) units balanced longest-first (dropkv_b200.sharding); every
+rank generates and runs only its own units, no collective on the data path;
+value = all units' positions / max over ranks of the device time (strong
+scaling: the total work is fixed).
+
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 numpy restatement in oracle/, the reference being Python with no compiled part)
 on the host cores, rank 0 only.
@@ -50,6 +57,12 @@ def parse_args():
     ap.add_argument("--keep-ratio", type=float, default=0.1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["layer", "ragged"], default="layer",
+                    help="layer: one Llama layer per rank (default, weak scaling); ragged: the "
+                         "config-5 batch split across ranks (strong scaling)")
+    ap.add_argument("--ragged-seqs", type=int, default=16)
+    ap.add_argument("--ragged-layers", type=int, default=32)
+    ap.add_argument("--ragged-seed", type=int, default=5)
     return ap.parse_args()
 
 
@@ -364,6 +377,93 @@ def run_ours(args, rank, n, world):
         print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# ragged batch (config 5) across ranks
+# ---------------------------------------------------------------------------
+RAGGED_METRIC = "KV positions scored+compacted/sec, ragged batch (config 5)"
+
+
+def run_ragged(args, rank, n, world):
+    import torch
+    import torch.distributed as dist
+    from dropkv_b200 import _lib, ops
+    from dropkv_b200.sharding import load_imbalance, lpt_partition, make_units, ragged_lengths
+    from dropkv_b200.workloads import llama_layer, make_qkv
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lengths = ragged_lengths(args.ragged_seqs, 4096, 65536, args.ragged_seed)
+    all_units = make_units(lengths, args.ragged_layers)
+    parts = lpt_partition(all_units, n)
+    mine = parts[rank]
+    comps, work = {}, []
+    for u in mine:
+        wl = llama_layer(u.lk, keep_ratio=args.keep_ratio, seed=1000 * u.seq + u.layer + 7)
+        if u.lk not in comps:
+            comps[u.lk] = ops.Compressor(wl.B, wl.Hq, wl.Hkv, wl.Lq, wl.Lk, wl.D, wl.dtype, wl.window_size,
+                                         wl.kernel_size, wl.keep_len(), device=dev)
+        work.append((comps[u.lk], make_qkv(wl, dev)))
+    stream = torch.cuda.current_stream(dev)
+
+    def one_pass():
+        for comp, (Q, K, V) in work:
+            comp.run(Q, K, V)
+
+    def barrier():
+        if world:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        one_pass()
+    barrier()
+    clocks = ClockSampler(gpu_uuid(dev))
+    clocks.start()
+    time.sleep(0.3)
+    n_launch0 = _lib.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        one_pass()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    launches = _lib.launch_count() - n_launch0
+    clk = clocks.stop()
+    total_ms = e0.elapsed_time(e1)
+    if world:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    if rank != 0:
+        return
+    ms_per_step = total_ms / args.steps
+    hkv = 8
+    positions = sum(hkv * u.lk for u in all_units)
+    value = positions * args.steps / (total_ms / 1e3)
+    path_bytes = sum(llama_layer(u.lk, keep_ratio=args.keep_ratio).algorithmic_bytes() for u in all_units)
+    peak, peak_kind = measured_peaks()
+    per_gpu_gbs = path_bytes / (ms_per_step / 1e3) / 1e9 / n
+    line = {
+        "metric": RAGGED_METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, config-2 value distribution per unit)",
+        "config": {"workload": f"ragged_b{args.ragged_seqs}_lk4096-65536_{args.ragged_layers}layers",
+                   "sequences_lk": lengths, "layers": args.ragged_layers, "Hq": 32, "Hkv": hkv, "D": 128,
+                   "Lq": 8, "window": 8, "kernel_size": 11, "keep_ratio": args.keep_ratio,
+                   "units": len(all_units), "units_per_rank": [len(p) for p in parts],
+                   "load_imbalance": load_imbalance(parts),
+                   "parallelism": f"{n} ranks, (sequence, layer) units, longest-first balance, no collective",
+                   "l2": "distinct inputs per unit, whole batch far above the 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": per_gpu_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": per_gpu_gbs / peak, "traffic": None,
+                     "kernel": "whole path (scores + select + gather), per GPU",
+                     "algorithmic_bytes": path_bytes, "ms": ms_per_step,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+        "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1")) > 1
@@ -380,7 +480,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
-        run_ours(args, rank, n, world)
+        if args.workload == "ragged":
+            run_ragged(args, rank, n, world)
+        else:
+            run_ours(args, rank, n, world)
     finally:
         if world:
             dist.destroy_process_group()
