@@ -22,6 +22,13 @@ rank generates and runs only its own units, no collective on the data path;
 value = all units' positions / max over ranks of the device time (strong
 scaling: the total work is fixed).
 
+``--workload chunked``: config 4 on one GPU -- 32 Llama layers whose cache
+grows to ``--lk`` (131072) in 4096-token chunks with Lq = 4096 tail-aligned
+queries per chunk, through the unchanged DropKVCache / prefill_chunked state
+machine (torch.cat storage as in the reference): (i) the last chunk of the
+``last_chunk`` strategy (every layer evicts its 131072-key cache) and (ii) the
+whole ``every_chunk`` prefill, device-timed with events around the calls.
+
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 numpy restatement in oracle/, the reference being Python with no compiled part)
 on the host cores, rank 0 only.
@@ -57,9 +64,12 @@ def parse_args():
     ap.add_argument("--keep-ratio", type=float, default=0.1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["layer", "ragged"], default="layer",
+    ap.add_argument("--workload", choices=["layer", "ragged", "chunked"], default="layer",
                     help="layer: one Llama layer per rank (default, weak scaling); ragged: the "
-                         "config-5 batch split across ranks (strong scaling)")
+                         "config-5 batch split across ranks (strong scaling); chunked: config-4 "
+                         "chunked prefill through DropKVCache / prefill_chunked (1 GPU)")
+    ap.add_argument("--chunked-layers", type=int, default=32)
+    ap.add_argument("--chunk", type=int, default=4096)
     ap.add_argument("--ragged-seqs", type=int, default=16)
     ap.add_argument("--ragged-layers", type=int, default=32)
     ap.add_argument("--ragged-seed", type=int, default=5)
@@ -464,6 +474,116 @@ def run_ragged(args, rank, n, world):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# chunked prefill (config 4) through the cache state machine
+# ---------------------------------------------------------------------------
+CHUNKED_METRIC = "KV positions scored+compacted/sec, chunked prefill (config 4)"
+
+
+class _ChunkModel:
+    """Stand-in for a causal LM: every layer writes the chunk's precomputed Q/K/V
+    (one contiguous K/V tensor per layer and chunk, as an attention layer makes)
+    into the cache through cache.update, like the reference's patched layers."""
+
+    def __init__(self, q_layers, kv_chunks, chunk):
+        self.q_layers, self.kv_chunks, self.chunk = q_layers, kv_chunks, chunk
+        self.pos = 0
+
+    def __call__(self, ids, past_key_values=None, use_cache=True):
+        n = ids.shape[1]
+        c = self.pos // self.chunk
+        for layer, q in enumerate(self.q_layers):
+            k, v = self.kv_chunks[layer][c]
+            past_key_values.update(q[:, :, :n], k[:, :, :n], v[:, :, :n], layer_idx=layer)
+        self.pos += n
+        return n
+
+
+def run_chunked(args):
+    import torch
+    from dropkv_b200 import DropKVCache, _lib, prefill_chunked
+    from dropkv_b200.workloads import llama_layer, make_qkv
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L, C, layers = args.lk, args.chunk, args.chunked_layers
+    n_chunks = (L + C - 1) // C
+    q_layers, kv_chunks = [], []
+    for layer in range(layers):
+        wl = llama_layer(L, keep_ratio=args.keep_ratio, seed=100 + layer, Lq=C)
+        Q, K, V = make_qkv(wl, dev)
+        q_layers.append(Q)
+        kv_chunks.append([(K[:, :, s:s + C].contiguous(), V[:, :, s:s + C].contiguous())
+                          for s in range(0, L, C)])
+        del K, V
+    ids = torch.zeros(1, L, dtype=torch.long)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(strategy, final_only):
+        cache = DropKVCache(keep_ratio=args.keep_ratio, window_size=8, kernel_size=11)
+        model = _ChunkModel(q_layers, kv_chunks, C)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if final_only:  # accumulate every chunk but the last untimed, then time the last
+            pre = _ChunkModel(q_layers, kv_chunks, C)
+            cache._prefill_mode = "accumulate"
+            for _ in range(n_chunks - 1):
+                pre(ids[:, :C], past_key_values=cache)
+            cache._prefill_mode = "evict_accumulated"
+            model.pos = pre.pos
+            torch.cuda.synchronize(dev)
+            n0 = _lib.launch_count()
+            e0.record(stream)
+            model(ids[:, :L - (n_chunks - 1) * C], past_key_values=cache)
+            e1.record(stream)
+            cache._prefill_mode = "single_pass"
+        else:
+            torch.cuda.synchronize(dev)
+            n0 = _lib.launch_count()
+            e0.record(stream)
+            prefill_chunked(model, ids, cache, chunk_size=C, evict_strategy=strategy)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1), _lib.launch_count() - n0, cache
+
+    for _ in range(max(1, args.warmup)):
+        timed("last_chunk", True)
+        timed("every_chunk", False)
+    last_ms, every_ms, launches = [], [], 0
+    for _ in range(args.steps):
+        t, nl, cache = timed("last_chunk", True)
+        last_ms.append(t)
+        launches += nl
+        kept = cache.key_cache[0].shape[2]
+        t, nl, _ = timed("every_chunk", False)
+        every_ms.append(t)
+        launches += nl
+    hkv = 8
+    last_pos = layers * hkv * L
+    # every_chunk: chunk i scores what is stored (keep_ratio of the tokens seen
+    # before it) plus the new chunk, and keeps keep_ratio of the tokens seen
+    every_pos, stored = 0, 0
+    for i in range(n_chunks):
+        new = min(C, L - i * C)
+        every_pos += layers * hkv * (stored + new)
+        seen = min(L, (i + 1) * C)
+        stored = min(stored + new, max(int(args.keep_ratio * seen), 8, 1))
+    lm, em = statistics.median(last_ms), statistics.median(every_ms)
+    line = {
+        "metric": CHUNKED_METRIC, "value": every_pos / (em / 1e3), "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": em, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, config-2 value distribution per layer)",
+        "config": {"workload": f"chunked_prefill_lk{L}_chunk{C}_{layers}layers", "Lk": L, "chunk": C,
+                   "Lq_per_chunk": C, "layers": layers, "Hq": 32, "Hkv": hkv, "D": 128,
+                   "keep_ratio": args.keep_ratio, "kept_per_layer_last_chunk": kept,
+                   "storage": "torch.cat per chunk (the reference's cache semantics)"},
+        "every_chunk": {"ms": em, "positions_scored": every_pos, "value": every_pos / (em / 1e3)},
+        "last_chunk_final": {"ms": lm, "positions_scored": last_pos, "value": last_pos / (lm / 1e3),
+                             "what": "the final chunk: per layer torch.cat to 131072 keys + eviction"},
+        "cpu_baseline": None, "e2e": None, "gpu_launches": launches // max(1, args.steps),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1")) > 1
@@ -471,6 +591,12 @@ def main():
     n = int(os.environ.get("WORLD_SIZE", str(args.gpus))) if world else 1
     if args.impl == "reference":
         run_reference(args, rank, n)
+        return
+    if args.workload == "chunked":
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        if rank == 0:
+            run_chunked(args)
         return
     import torch
     import torch.distributed as dist
