@@ -70,6 +70,8 @@ def parse_args():
                          "chunked prefill through DropKVCache / prefill_chunked (1 GPU)")
     ap.add_argument("--chunked-layers", type=int, default=32)
     ap.add_argument("--chunk", type=int, default=4096)
+    ap.add_argument("--storage", choices=["cat", "buffer"], default="cat",
+                    help="chunked mode: DropKVCache storage (cat: the reference's; buffer: row buffers)")
     ap.add_argument("--ragged-seqs", type=int, default=16)
     ap.add_argument("--ragged-layers", type=int, default=32)
     ap.add_argument("--ragged-seed", type=int, default=5)
@@ -519,7 +521,7 @@ def run_chunked(args):
     stream = torch.cuda.current_stream(dev)
 
     def timed(strategy, final_only):
-        cache = DropKVCache(keep_ratio=args.keep_ratio, window_size=8, kernel_size=11)
+        cache = DropKVCache(keep_ratio=args.keep_ratio, window_size=8, kernel_size=11, storage=args.storage)
         model = _ChunkModel(q_layers, kv_chunks, C)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if final_only:  # accumulate every chunk but the last untimed, then time the last
@@ -544,15 +546,35 @@ def run_chunked(args):
         torch.cuda.synchronize(dev)
         return e0.elapsed_time(e1), _lib.launch_count() - n0, cache
 
+    # decode steps on the compressed cache: one token per layer and step through
+    # cache.update (the storage's append; attention itself is not part of the path)
+    dec_q = [q[:, :, -1:].contiguous() for q in q_layers]
+    dec_kv = [(kv[-1][0][:, :, -1:].contiguous(), kv[-1][1][:, :, -1:].contiguous()) for kv in kv_chunks]
+    n_dec = 64
+
+    def decode(cache):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for _ in range(n_dec):
+            for layer in range(layers):
+                cache.update(dec_q[layer], dec_kv[layer][0], dec_kv[layer][1], layer_idx=layer)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n_dec
+
     for _ in range(max(1, args.warmup)):
-        timed("last_chunk", True)
+        _, _, c = timed("last_chunk", True)
+        decode(c)
         timed("every_chunk", False)
-    last_ms, every_ms, launches = [], [], 0
+    last_ms, every_ms, dec_ms, launches = [], [], [], 0
     for _ in range(args.steps):
         t, nl, cache = timed("last_chunk", True)
         last_ms.append(t)
         launches += nl
         kept = cache.key_cache[0].shape[2]
+        dec_ms.append(decode(cache))
+        del cache
         t, nl, _ = timed("every_chunk", False)
         every_ms.append(t)
         launches += nl
@@ -575,10 +597,14 @@ def run_chunked(args):
         "config": {"workload": f"chunked_prefill_lk{L}_chunk{C}_{layers}layers", "Lk": L, "chunk": C,
                    "Lq_per_chunk": C, "layers": layers, "Hq": 32, "Hkv": hkv, "D": 128,
                    "keep_ratio": args.keep_ratio, "kept_per_layer_last_chunk": kept,
-                   "storage": "torch.cat per chunk (the reference's cache semantics)"},
+                   "storage": ("torch.cat per chunk (the reference's cache semantics)" if args.storage == "cat"
+                               else "row buffers: in-place append, eviction into the other buffer")},
         "every_chunk": {"ms": em, "positions_scored": every_pos, "value": every_pos / (em / 1e3)},
         "last_chunk_final": {"ms": lm, "positions_scored": last_pos, "value": last_pos / (lm / 1e3),
-                             "what": "the final chunk: per layer torch.cat to 131072 keys + eviction"},
+                             "what": "the final chunk: per layer the append to 131072 keys + eviction"},
+        "decode_append": {"ms_per_token_step": statistics.median(dec_ms), "layers": layers,
+                          "what": f"{n_dec} decode steps after the last_chunk prefill, one token per layer "
+                                  "through cache.update (storage only, no attention)"},
         "cpu_baseline": None, "e2e": None, "gpu_launches": launches // max(1, args.steps),
     }
     print(json.dumps(line), flush=True)

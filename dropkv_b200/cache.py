@@ -23,7 +23,7 @@ from typing import Any, Optional
 
 import torch
 
-from . import ops
+from . import _lib, ops
 
 logger = logging.getLogger(__name__)
 
@@ -173,12 +173,117 @@ class DynamicCache(Cache):
 _VALID_MODES = ("single_pass", "accumulate", "evict_accumulated")
 
 
+class _LayerRows:
+    """One layer's K/V for ``DropKVCache(storage="buffer")``: two [B, Hkv, capacity, D]
+    buffer pairs used in turn.  Rows [0, n) of the current pair are the layer's
+    cache.  New tokens are copied in place after them (the reference concatenates
+    stored and new K/V into fresh tensors for every chunk and decode step,
+    dropkv_cache.py:581-617).  An eviction scores the current pair's rows and writes
+    the kept rows to the other pair, which becomes current; the evicted-from rows
+    stay intact until the pair is written again, so the full K/V returned for the
+    chunk's attention remains valid until the layer's next update.  Each pair grows
+    (doubling, one copy of its live rows) only when it must hold more rows."""
+
+    def __init__(self, like: torch.Tensor):
+        self.shape = (like.shape[0], like.shape[1], like.shape[3])
+        self.dtype, self.device = like.dtype, like.device
+        self.bufs: list = [None, None]
+        self.cur = 0
+        self.n = 0
+        self.last_m = 0  # rows of the last append: an eviction target keeps room for the next one
+        self.ws = torch.empty(0, dtype=torch.uint8, device=self.device)    # reused scratch
+        self.idx = torch.empty(0, dtype=torch.int64, device=self.device)   # reused keep indices
+
+    def _alloc(self, rows: int):
+        B, H, D = self.shape
+        return (torch.empty(B, H, rows, D, dtype=self.dtype, device=self.device),
+                torch.empty(B, H, rows, D, dtype=self.dtype, device=self.device))
+
+    def _reserve(self, which: int, rows: int, keep_live: bool):
+        buf = self.bufs[which]
+        have = 0 if buf is None else buf[0].shape[2]
+        if rows <= have:
+            return
+        new = self._alloc(-(-max(rows, 2 * have) // 1024) * 1024)
+        if keep_live and buf is not None and self.n:
+            new[0][:, :, :self.n].copy_(buf[0][:, :, :self.n])
+            new[1][:, :, :self.n].copy_(buf[1][:, :, :self.n])
+        self.bufs[which] = new
+
+    def views(self):
+        k, v = self.bufs[self.cur]
+        return k[:, :, :self.n], v[:, :, :self.n]
+
+    def append(self, k_new: torch.Tensor, v_new: torch.Tensor):
+        m = k_new.shape[2]
+        self.last_m = max(self.last_m, m)
+        self._reserve(self.cur, self.n + m, keep_live=True)
+        k, v = self.bufs[self.cur]
+        if k.is_cuda and k_new.is_cuda and k_new.is_contiguous() and v_new.is_contiguous() and \
+                k_new.dtype == k.dtype and v_new.dtype == k.dtype:
+            B, H, D = self.shape
+            with torch.cuda.device(self.device):
+                rc = _lib.load().dropkv_append_rows(
+                    k.data_ptr(), v.data_ptr(), k.shape[2] * D, self.n, k_new.data_ptr(), v_new.data_ptr(),
+                    m * D, m, D, k.element_size(), B * H, torch.cuda.current_stream(self.device).cuda_stream)
+            _lib.check(rc, "dropkv_append_rows")
+        else:  # CPU tensors or non-contiguous chunks
+            k[:, :, self.n:self.n + m].copy_(k_new)
+            v[:, :, self.n:self.n + m].copy_(v_new)
+        self.n += m
+
+    def _compress(self, q, k, v, lk, window, kernel_size, keep_len, ko, vo, protect):
+        """dropkv_compress_strided on these buffers (shapes are guaranteed by the
+        cache, so the call skips the generic wrapper's checks and allocations)."""
+        B, H, D = self.shape
+        lib = _lib.load()
+        need = lib.dropkv_compress_workspace_size(B, q.shape[1], H, lk, D, window)
+        if self.ws.numel() < need:
+            self.ws = torch.empty(max(need, 2 * self.ws.numel()), dtype=torch.uint8, device=self.device)
+        if self.idx.numel() < B * H * keep_len:
+            self.idx = torch.empty(max(B * H * keep_len, 2 * self.idx.numel()), dtype=torch.int64,
+                                   device=self.device)
+        if q.dtype != self.dtype or not q.is_cuda:
+            raise TypeError("query_states must be a CUDA tensor of the cache's dtype")
+        with torch.cuda.device(self.device):
+            rc = lib.dropkv_compress_strided(
+                q.data_ptr(), *q.stride(), q.shape[2], k.data_ptr(), v.data_ptr(), k.shape[2] * D,
+                ops._DTYPE_CODE[self.dtype], B, q.shape[1], H, lk, D, window, 1e-6, ops._ROUND_CODE[self.dtype],
+                kernel_size, protect, keep_len, None, self.idx.data_ptr(), ko.data_ptr(), vo.data_ptr(),
+                ko.shape[2] * D, self.ws.data_ptr(), self.ws.numel(),
+                torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc, "dropkv_compress_strided")
+
+    def evict(self, q: torch.Tensor, window: int, kernel_size: int, keep_len: int, protect: int):
+        other = 1 - self.cur
+        self._reserve(other, keep_len + self.last_m, keep_live=False)
+        (k, v), (ko, vo) = self.bufs[self.cur], self.bufs[other]
+        self._compress(q, k, v, self.n, window, kernel_size, keep_len, ko, vo, protect)
+        self.cur, self.n = other, keep_len
+
+    def load_evicted(self, q, k, v, window: int, kernel_size: int, keep_len: int, protect: int):
+        """First eviction of a layer, straight from the model's contiguous K/V."""
+        self._reserve(self.cur, keep_len, keep_live=False)
+        ko, vo = self.bufs[self.cur]
+        self._compress(q, k, v, k.shape[2], window, kernel_size, keep_len, ko, vo, protect)
+        self.n = keep_len
+
+
 class DropKVCache(DynamicCache):
     """KV cache that evicts at prefill with the DropKV score (CUDA backend)."""
 
     def __init__(self, keep_ratio: float = 0.1, window_size: int = 8, kernel_size: int = 11,
-                 use_triton: bool = True) -> None:
+                 use_triton: bool = True, storage: str = "cat") -> None:
+        """``storage``: ``"cat"`` (default) keeps the reference's storage, a fresh
+        tensor per layer after every update; ``"buffer"`` keeps each layer in
+        preallocated row buffers (no copy of the stored cache per chunk or decode
+        step).  With ``"buffer"`` the tensors in key_cache / value_cache and those
+        update returns are views that stay valid until that layer's next update."""
         super().__init__()
+        if storage not in ("cat", "buffer"):
+            raise ValueError(f"storage must be 'cat' or 'buffer', got {storage!r}")
+        self.storage = storage
+        self._rows: list[_LayerRows] = []
         if not 0 < keep_ratio <= 1.0:
             raise ValueError(f"keep_ratio must be in (0, 1], got {keep_ratio}")
         if window_size <= 0:
@@ -193,6 +298,30 @@ class DropKVCache(DynamicCache):
         self._prefill_mode = "single_pass"
         self._evict_use_seen_tokens = False
         self._budget_max_kv_tokens: Optional[int] = None
+
+    def _rebuild_rows(self):
+        """Row buffers again from key_cache / value_cache after they were replaced
+        by a whole-cache operation (crop, batch reordering)."""
+        if self.storage != "buffer":
+            return
+        self._rows = []
+        for i in range(len(self.key_cache)):
+            rows = _LayerRows(self.key_cache[i])
+            rows.append(self.key_cache[i], self.value_cache[i])
+            self._rows.append(rows)
+            self.key_cache[i], self.value_cache[i] = rows.views()
+
+    def crop(self, max_length: int):
+        super().crop(max_length)
+        self._rebuild_rows()
+
+    def batch_repeat_interleave(self, repeats: int):
+        super().batch_repeat_interleave(repeats)
+        self._rebuild_rows()
+
+    def batch_select_indices(self, indices: torch.Tensor):
+        super().batch_select_indices(indices)
+        self._rebuild_rows()
 
     def batch_split(self, full_batch_size: int, split_size: int):
         raise NotImplementedError(
@@ -236,11 +365,40 @@ class DropKVCache(DynamicCache):
         """dropkv_cache.py:479-491."""
         return ops.gather_compressed(key_states, value_states, keep_idx)
 
+    def _evict_keep_len(self, seq_len: int) -> int:
+        total = self._seen_tokens if self._evict_use_seen_tokens else None
+        return self._keep_len(seq_len, total, self._budget_max_kv_tokens)
+
+    def _store_new(self, key_states, value_states):
+        """A layer's first K/V, kept without eviction."""
+        if self.storage == "buffer":
+            rows = _LayerRows(key_states)
+            rows.append(key_states, value_states)
+            self._rows.append(rows)
+            key_states, value_states = rows.views()
+        self.key_cache.append(key_states)
+        self.value_cache.append(value_states)
+
+    def _update_rows(self, query_states, key_states, value_states, layer_idx):
+        """The continuation branches of update (dropkv_cache.py:576-622) over row
+        buffers: same decisions, same kept rows, no concatenation."""
+        rows = self._rows[layer_idx]
+        mode = self._prefill_mode
+        if mode not in _VALID_MODES:
+            raise ValueError(f"Invalid _prefill_mode {mode!r} in decode path")
+        rows.append(key_states, value_states)
+        full_k, full_v = rows.views()
+        if mode == "evict_accumulated" and query_states is not None and rows.n >= self.window_size:
+            self._check_heads(query_states, full_k)
+            W = min(self.window_size, query_states.shape[2])
+            rows.evict(query_states, W, self.kernel_size, self._evict_keep_len(rows.n), self.window_size)
+        self.key_cache[layer_idx], self.value_cache[layer_idx] = rows.views()
+        return full_k, full_v
+
     def _evict(self, query_states, key_states, value_states):
         """Fused _compute_keep_indices + _gather_compressed: one C-ABI call."""
         self._check_heads(query_states, key_states)
-        total = self._seen_tokens if self._evict_use_seen_tokens else None
-        kl = self._keep_len(key_states.shape[2], total, self._budget_max_kv_tokens)
+        kl = self._evict_keep_len(key_states.shape[2])
         W = min(self.window_size, query_states.shape[2])
         _, kc, vc = ops.compress(query_states, key_states, value_states, W, self.kernel_size, kl,
                                  protect_window=self.window_size)
@@ -271,19 +429,31 @@ class DropKVCache(DynamicCache):
             if query_states is None:
                 if self._prefill_mode != "single_pass":
                     logger.warning("query_states is None at layer %d — storing full KV without eviction.", layer_idx)
-                self.key_cache.append(key_states)
-                self.value_cache.append(value_states)
+                self._store_new(key_states, value_states)
                 return key_states, value_states
             if self._prefill_mode not in _VALID_MODES:
                 raise ValueError(f"Invalid _prefill_mode: {self._prefill_mode!r}")
             if self._prefill_mode == "accumulate" or key_states.shape[2] < self.window_size:
-                self.key_cache.append(key_states)
-                self.value_cache.append(value_states)
+                self._store_new(key_states, value_states)
+                return key_states, value_states
+            if self.storage == "buffer":
+                rows = _LayerRows(key_states)
+                kl = self._evict_keep_len(key_states.shape[2])
+                W = min(self.window_size, query_states.shape[2])
+                self._check_heads(query_states, key_states)
+                rows.load_evicted(query_states, key_states.contiguous(), value_states.contiguous(), W,
+                                  self.kernel_size, kl, self.window_size)
+                self._rows.append(rows)
+                kv, vv = rows.views()
+                self.key_cache.append(kv)
+                self.value_cache.append(vv)
                 return key_states, value_states
             kc, vc = self._evict(query_states, key_states, value_states)
             self.key_cache.append(kc)
             self.value_cache.append(vc)
             return key_states, value_states
+        if self.storage == "buffer":
+            return self._update_rows(query_states, key_states, value_states, layer_idx)
 
         # continuation: decode or chunked prefill
         mode = self._prefill_mode
@@ -381,6 +551,7 @@ def prefill_chunked(model, input_ids, cache, chunk_size=4096, evict_strategy="la
     except BaseException:
         cache.key_cache.clear()
         cache.value_cache.clear()
+        cache._rows.clear()
         cache._seen_tokens = 0
         raise
     finally:

@@ -114,7 +114,7 @@ static ScoreProblem make_problem(const void* q, int64_t q_sb, int64_t q_sh, int6
                                  int D, int window, float eps, int round_p, float* scores) {
   ScoreProblem p;
   p.q = q; p.q_sb = q_sb; p.q_sh = q_sh; p.q_ss = q_ss; p.q_sd = q_sd; p.Lq = Lq;
-  p.k = k; p.v = v; p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.Lk = Lk; p.D = D;
+  p.k = k; p.v = v; p.kv_sh = (int64_t)Lk * D; p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.Lk = Lk; p.D = D;
   p.W = window; p.g = Hq / Hkv; p.M = p.g * window;
   p.scale = (float)(1.0 / std::sqrt((double)D));
   p.eps = eps; p.round_mode = round_p; p.scores = scores;
@@ -320,6 +320,67 @@ int dropkv_compress(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int
                                 elem_bytes_of(dtype), D, k_out, v_out, st);
   if ((rc = launch_select(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, sel_ws, st))) return rc;
   return launch_gather(k, v, elem_bytes_of(dtype), B * Hkv, Lk, D, keep_idx, keep_len, k_out, v_out, st);
+}
+
+int dropkv_compress_strided(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                            const void* k, const void* v, int64_t kv_head_stride, int dtype, int B, int Hq,
+                            int Hkv, int Lk, int D, int window, float eps, int round_p, int kernel_size,
+                            int protect_window, int keep_len, float* scores_out, int64_t* keep_idx,
+                            void* k_out, void* v_out, int64_t out_head_stride, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  int rc = check_score_args(q, Lq, k, v, dtype, B, Hq, Hkv, Lk, D, window, round_p);
+  if (rc) return rc;
+  if ((rc = check_select_args(B, Hkv, Lk, kernel_size, protect_window, keep_len))) return rc;
+  if (!keep_idx || !k_out || !v_out) return fail(DROPKV_ERR_ARG, "keep_idx, k_out and v_out must be non-NULL");
+  if (kv_head_stride < (int64_t)Lk * D || kv_head_stride % 8)
+    return fail(DROPKV_ERR_ARG, "kv_head_stride (%lld) must be >= Lk*D (%lld) and a multiple of 8",
+                (long long)kv_head_stride, (long long)Lk * D);
+  if (out_head_stride < (int64_t)keep_len * D || out_head_stride % 8)
+    return fail(DROPKV_ERR_ARG, "out_head_stride (%lld) must be >= keep_len*D (%lld) and a multiple of 8",
+                (long long)out_head_stride, (long long)keep_len * D);
+  if (reinterpret_cast<uintptr_t>(k_out) % 16 || reinterpret_cast<uintptr_t>(v_out) % 16)
+    return fail(DROPKV_ERR_ARG, "k_out and v_out must be 16-byte aligned");
+  size_t s_ws = dropkv_scores_workspace_size(B, Hq, Hkv, Lk, D, window);
+  size_t need = dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, window);
+  if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
+  char* base = reinterpret_cast<char*>(workspace);
+  float* scores = scores_out ? scores_out : reinterpret_cast<float*>(base + s_ws);
+  void* sel_ws = base + s_ws + align_up((size_t)B * Hkv * Lk * 4, 256);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ScoreProblem p = make_problem(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, B, Hq, Hkv, Lk, D, window, eps,
+                                round_p, scores);
+  p.kv_sh = kv_head_stride;
+  if ((rc = run_scores(p, dtype, workspace, st))) return rc;
+  int protect = std::min(protect_window, Lk);
+  if (select_gather_supported(Lk, kernel_size))
+    return launch_select_gather(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, k, v,
+                                elem_bytes_of(dtype), D, k_out, v_out, st, kv_head_stride, out_head_stride);
+  if ((rc = launch_select(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, sel_ws, st))) return rc;
+  return launch_gather(k, v, elem_bytes_of(dtype), B * Hkv, Lk, D, keep_idx, keep_len, k_out, v_out, st,
+                       kv_head_stride, out_head_stride);
+}
+
+int dropkv_append_rows(void* k_dst, void* v_dst, int64_t dst_head_stride, int dst_row, const void* k_src,
+                       const void* v_src, int64_t src_head_stride, int rows, int D, int elem_bytes, int BH,
+                       void* stream) {
+  if (!k_dst || !v_dst || !k_src || !v_src) return fail(DROPKV_ERR_ARG, "NULL pointer argument");
+  if (elem_bytes != 2 && elem_bytes != 4) return fail(DROPKV_ERR_ARG, "elem_bytes must be 2 or 4");
+  if (rows < 0 || D < 1 || BH < 1 || dst_row < 0) return fail(DROPKV_ERR_ARG, "invalid append sizes");
+  if (src_head_stride < (int64_t)rows * D || dst_head_stride < (int64_t)(dst_row + rows) * D)
+    return fail(DROPKV_ERR_ARG, "head strides too small for the rows");
+  if (rows == 0) return DROPKV_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t width = (size_t)rows * D * elem_bytes;
+  const size_t off = (size_t)dst_row * D * elem_bytes;
+  for (int t = 0; t < 2; ++t) {
+    char* dst = reinterpret_cast<char*>(t ? v_dst : k_dst) + off;
+    const void* src = t ? v_src : k_src;
+    cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)dst_head_stride * elem_bytes, src,
+                                      (size_t)src_head_stride * elem_bytes, width, (size_t)BH,
+                                      cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "append copy: %s", cudaGetErrorString(e));
+  }
+  return DROPKV_OK;
 }
 
 }  // extern "C"

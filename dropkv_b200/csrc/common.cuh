@@ -60,6 +60,7 @@ struct ScoreProblem {
   int Lq;
   const void* k;
   const void* v;
+  int64_t kv_sh;  // elements between consecutive (b, kv head) rows of K and V (Lk * D if contiguous)
   int B, Hq, Hkv, Lk, D;
   int W;       // query rows per head used (window)
   int g;       // Hq / Hkv
@@ -103,11 +104,13 @@ int launch_select(const float* scores, int BH, int Lk, int kernel_size, int prot
                   int64_t* keep_idx, void* ws, cudaStream_t st);
 bool select_gather_supported(int Lk, int kernel_size);
 // k == nullptr: selection only (keep_idx), no gather
+// in_sh / out_sh: elements between consecutive heads of K/V and of K_c/V_c
+// (0: contiguous, Lk * D and keep_len * D)
 int launch_select_gather(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
                          int64_t* keep_idx, const void* k, const void* v, int elem_bytes, int D, void* ko,
-                         void* vo, cudaStream_t st);
+                         void* vo, cudaStream_t st, int64_t in_sh = 0, int64_t out_sh = 0);
 int launch_gather(const void* k, const void* v, int elem_bytes, int BH, int Lk, int D,
                   const int64_t* keep_idx, int keep_len, void* k_out, void* v_out,
-                  cudaStream_t st);
+                  cudaStream_t st, int64_t in_sh = 0, int64_t out_sh = 0);
 
 }  // namespace dropkv

@@ -93,8 +93,8 @@ __global__ void __launch_bounds__(NT) fwd_partial_kernel(ScoreProblem p, ScorePl
   const int b = bh / p.Hkv, hkv = bh % p.Hkv;
   const int tid = threadIdx.x;
   const int r = tid >> 3, sub = tid & 7;
-  const T* kh = reinterpret_cast<const T*>(p.k) + (size_t)bh * p.Lk * D;
-  const T* vh = reinterpret_cast<const T*>(p.v) + (size_t)bh * p.Lk * D;
+  const T* kh = reinterpret_cast<const T*>(p.k) + (size_t)bh * p.kv_sh;
+  const T* vh = reinterpret_cast<const T*>(p.v) + (size_t)bh * p.kv_sh;
 
   const int t_begin = s_idx * plan.tps;
   const int t_end = min(t_begin + plan.tps, plan.tiles);
@@ -255,8 +255,8 @@ __global__ void __launch_bounds__(NT) score_kernel(ScoreProblem p, ScorePlan pla
   const int warp = tid >> 5, lane = tid & 31;
   const int r = tid >> 3, sub = tid & 7;
   const int base = tile * TJ;
-  const T* kh = reinterpret_cast<const T*>(p.k) + (size_t)bh * p.Lk * D;
-  const T* vh = reinterpret_cast<const T*>(p.v) + (size_t)bh * p.Lk * D;
+  const T* kh = reinterpret_cast<const T*>(p.k) + (size_t)bh * p.kv_sh;
+  const T* vh = reinterpret_cast<const T*>(p.v) + (size_t)bh * p.kv_sh;
   const float* lse = ws + plan.off_lse / 4;
   const float* yn = ws + plan.off_yn / 4;
   const float* yg = ws + plan.off_y / 4;

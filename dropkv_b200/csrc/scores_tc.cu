@@ -62,12 +62,14 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int make_kv_tensor_map(CUtensorMap* map, const void* base, int BH, int L, int D, bool bf16) {
+int make_kv_tensor_map(CUtensorMap* map, const void* base, int BH, int L, int D, bool bf16, int64_t head_stride) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(DROPKV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   if (reinterpret_cast<uintptr_t>(base) % 16) return fail(DROPKV_ERR_ARG, "K/V must be 16-byte aligned");
+  const int64_t hs = head_stride ? head_stride : (int64_t)L * D;
+  if ((hs * 2) % 16) return fail(DROPKV_ERR_ARG, "K/V head stride must be a multiple of 8 elements");
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)L, (cuuint64_t)BH};
-  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)L * D * 2};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)hs * 2};
   cuuint32_t box[3] = {64, 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
@@ -1013,9 +1015,9 @@ static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cuda
   CUtensorMap km, vm;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   const int BH = p.B * p.Hkv;
-  int rc = make_kv_tensor_map(&km, p.k, BH, p.Lk, D, bf16);
+  int rc = make_kv_tensor_map(&km, p.k, BH, p.Lk, D, bf16, p.kv_sh);
   if (rc) return rc;
-  rc = make_kv_tensor_map(&vm, p.v, BH, p.Lk, D, bf16);
+  rc = make_kv_tensor_map(&vm, p.v, BH, p.Lk, D, bf16, p.kv_sh);
   if (rc) return rc;
   CUtensorMap qm;
   std::memset(&qm, 0, sizeof(qm));

@@ -396,10 +396,10 @@ static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel
 // Selection into keep_idx and, when K/V are given, the gather of the kept rows.
 int launch_select_gather(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
                          int64_t* keep_idx, const void* k, const void* v, int elem_bytes, int D, void* ko,
-                         void* vo, cudaStream_t st) {
+                         void* vo, cudaStream_t st, int64_t in_sh, int64_t out_sh) {
   int rc = launch_cluster_select(scores, BH, Lk, kernel_size, protect, keep_len, keep_idx, st);
   if (rc || k == nullptr) return rc;
-  return launch_gather(k, v, elem_bytes, BH, Lk, D, keep_idx, keep_len, ko, vo, st);
+  return launch_gather(k, v, elem_bytes, BH, Lk, D, keep_idx, keep_len, ko, vo, st, in_sh, out_sh);
 }
 
 }  // namespace dropkv

@@ -267,6 +267,7 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a
 
 // Host: encode a 3-D TMA descriptor for a contiguous [BH, L, D] 16-bit tensor,
 // box {64 elements, 128 rows, 1}, 128-byte swizzle, out-of-range rows zero-filled.
-int make_kv_tensor_map(CUtensorMap* map, const void* base, int BH, int L, int D, bool bf16);
+// head_stride: elements between consecutive [L, D] heads (0: L * D, contiguous).
+int make_kv_tensor_map(CUtensorMap* map, const void* base, int BH, int L, int D, bool bf16, int64_t head_stride = 0);
 
 }  // namespace dropkv

@@ -9,6 +9,8 @@
 * ``select_keep_indices`` -- pool + protect + top-k + sort (dropkv_cache.py:462-477).
 * ``gather_compressed``  -- dropkv_cache.py:479-491.
 * ``compress``           -- the whole path in one C call.
+* ``compress_strided``   -- the same over preallocated row buffers (in-place
+  chunked prefill storage, no concatenation).
 """
 
 from __future__ import annotations
@@ -207,6 +209,61 @@ def compress(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int, ker
     if return_scores:
         return idx, Kc, Vc, sc
     return idx, Kc, Vc
+
+
+def compress_workspace_size(B: int, Hq: int, Hkv: int, Lk: int, D: int, window: int) -> int:
+    """Scratch bytes of compress / compress_strided for this problem."""
+    return int(_lib.load().dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, int(window)))
+
+
+def compress_strided(Q: torch.Tensor, K_buf: torch.Tensor, V_buf: torch.Tensor, Lk: int, window: int,
+                     kernel_size: int, keep_len: int, K_out: torch.Tensor, V_out: torch.Tensor,
+                     protect_window: int | None = None, eps: float = 1e-6, round_p: bool = True,
+                     workspace: torch.Tensor | None = None, idx_out: torch.Tensor | None = None) -> torch.Tensor:
+    """``compress`` over row buffers: scores the first ``Lk`` rows of ``K_buf`` /
+    ``V_buf`` ([B, Hkv, capacity, D], contiguous) and writes the kept rows to rows
+    ``[0, keep_len)`` of ``K_out`` / ``V_out`` ([B, Hkv, capacity', D], contiguous,
+    not the input buffers).  Returns keep_idx [B, Hkv, keep_len] (ascending).
+    Same results as ``compress`` on the same rows; nothing is concatenated.
+    ``workspace`` (uint8, large enough) and ``idx_out`` (int64, at least
+    B * Hkv * keep_len elements) are used instead of allocating when given."""
+    _require_cuda(Q, K_buf, V_buf, K_out, V_out)
+    B, Hq, Lq, D = Q.shape
+    Bk, Hkv, cap, Dk = K_buf.shape
+    dt = _DTYPE_CODE.get(Q.dtype)
+    if dt is None or K_buf.dtype != Q.dtype or V_buf.dtype != Q.dtype or K_out.dtype != Q.dtype:
+        raise TypeError("Q, K/V buffers and outputs must share one of fp32/fp16/bf16")
+    for t in (K_buf, V_buf, K_out, V_out):
+        if not t.is_contiguous():
+            raise ValueError("row buffers must be contiguous [B, Hkv, capacity, D]")
+    if K_buf.shape != V_buf.shape or K_out.shape != V_out.shape or Bk != B or Dk != D:
+        raise ValueError("buffer shapes disagree")
+    if not 1 <= Lk <= cap or keep_len > K_out.shape[2]:
+        raise ValueError(f"Lk={Lk} must fit the input buffer ({cap} rows) and keep_len={keep_len} the "
+                         f"output buffer ({K_out.shape[2]} rows)")
+    if K_out.data_ptr() == K_buf.data_ptr():
+        raise ValueError("K_out must not be the input buffer")
+    pw = window if protect_window is None else protect_window
+    lib = _lib.load()
+    dev = Q.device
+    with torch.cuda.device(dev):
+        n_idx = B * Hkv * keep_len
+        if idx_out is not None and idx_out.dtype == torch.int64 and idx_out.numel() >= n_idx and idx_out.is_contiguous():
+            idx = idx_out.view(-1)[:n_idx].view(B, Hkv, keep_len)
+        else:
+            idx = torch.empty(B, Hkv, keep_len, dtype=torch.int64, device=dev)
+        need = lib.dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, int(window))
+        ws = workspace if workspace is not None and workspace.numel() >= need else _workspace(need, dev)
+        rc = lib.dropkv_compress_strided(Q.data_ptr(), *Q.stride(), Lq, K_buf.data_ptr(), V_buf.data_ptr(),
+                                         cap * D, dt, B, Hq, Hkv, int(Lk), D, int(window), float(eps),
+                                         _ROUND_CODE[Q.dtype] if round_p else _lib.ROUND_NONE,
+                                         int(kernel_size), int(pw), int(keep_len), None, idx.data_ptr(),
+                                         K_out.data_ptr(), V_out.data_ptr(), K_out.shape[2] * D,
+                                         ws.data_ptr(), ws.numel(), _stream(dev))
+        _lib.check(rc, "dropkv_compress_strided")
+        if _CHECK_STATUS:
+            _check_status(ws, dt, B, Hq, Hkv, Lk, D, window, "dropkv_compress_strided")
+    return idx
 
 
 def inv_sqrt_d(D: int) -> float:

@@ -25,6 +25,7 @@
  *   dropkv_select          <- dropkv_cache.py:462-477   max_pool1d + protect + topk + sort
  *   dropkv_gather          <- dropkv_cache.py:479-491   DropKVCache._gather_compressed
  *   dropkv_compress        <- dropkv_cache.py:355-491   _compute_keep_indices + _gather_compressed
+ *   dropkv_compress_strided <- dropkv_cache.py:581-607  the same over in-place row buffers (no torch.cat)
  */
 #ifndef DROPKV_B200_H
 #define DROPKV_B200_H
@@ -156,6 +157,32 @@ DROPKV_API int dropkv_compress(const void* q, int64_t q_sb, int64_t q_sh, int64_
                     int window, float eps, int round_p, int kernel_size, int protect_window,
                     int keep_len, float* scores_out, int64_t* keep_idx, void* k_out, void* v_out,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* dropkv_compress for K/V kept in preallocated per-layer row buffers: K and V
+ * are [B, Hkv, capacity, D] with kv_head_stride = capacity * D elements between
+ * consecutive (b, kv head) rows (>= Lk * D, a multiple of 8); their first Lk rows
+ * are scored.  The kept rows go to k_out / v_out laid out the same way with
+ * out_head_stride elements between heads (>= keep_len * D, a multiple of 8; may be
+ * the other buffer of a ping-pong pair, not the input itself).  Lets a chunked
+ * prefill append each chunk in place and compact in place instead of copying the
+ * whole cache per chunk as the reference's storage does
+ * (dropkv_cache.py:581-607: torch.cat of stored + new K/V before every
+ * eviction).  Results equal dropkv_compress on the same rows. */
+DROPKV_API int dropkv_compress_strided(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd,
+                                       int Lq, const void* k, const void* v, int64_t kv_head_stride, int dtype,
+                                       int B, int Hq, int Hkv, int Lk, int D, int window, float eps, int round_p,
+                                       int kernel_size, int protect_window, int keep_len, float* scores_out,
+                                       int64_t* keep_idx, void* k_out, void* v_out, int64_t out_head_stride,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Appends `rows` rows per (b, kv head) of K and V (src: [BH, rows, D] with
+ * src_head_stride elements between heads) at row dst_row of row buffers with
+ * dst_head_stride elements between heads: one pitched device copy per tensor.
+ * No counterpart in the reference, which concatenates the stored cache and the
+ * new tokens into new tensors instead (dropkv_cache.py:581-617). */
+DROPKV_API int dropkv_append_rows(void* k_dst, void* v_dst, int64_t dst_head_stride, int dst_row,
+                                  const void* k_src, const void* v_src, int64_t src_head_stride, int rows,
+                                  int D, int elem_bytes, int BH, void* stream);
 
 /* Diagnostic: one 128-row tile through a tcgen05 MMA form used by the fused
  * scorer (mode 0: out[128][n] = A[128][128] B[n][128]^T with A loaded by TMA;

@@ -190,3 +190,26 @@ def test_dynamic_cache_helpers():
     assert torch.equal(c2.key_cache[0], c.key_cache[0])
     c2.crop(10)
     assert c2.get_seq_length() == 10
+
+
+@pytest.mark.parametrize("storage", ["cat", "buffer"])
+def test_buffer_storage_non_evicting_paths_on_cpu(storage):
+    """Accumulating prefill and decode appends need no GPU: the row buffers must
+    hold exactly what the concatenating storage holds."""
+    torch.manual_seed(0)
+    K = torch.randn(1, 2, 40, 16)
+    V = torch.randn(1, 2, 40, 16)
+    c = DropKVCache(keep_ratio=0.5, storage=storage)
+    c._prefill_mode = "accumulate"
+    for s in range(0, 32, 8):
+        c.update(None, K[:, :, s:s + 8], V[:, :, s:s + 8], layer_idx=0)
+    c._prefill_mode = "single_pass"
+    for t in range(32, 40):
+        rk, rv = c.update(None, K[:, :, t:t + 1], V[:, :, t:t + 1], layer_idx=0)
+    assert torch.equal(c.key_cache[0], K) and torch.equal(c.value_cache[0], V)
+    assert torch.equal(rk, K) and torch.equal(rv, V)
+    c.crop(30)
+    c.update(None, K[:, :, :1], V[:, :, :1], layer_idx=0)
+    assert torch.equal(c.key_cache[0], torch.cat([K[:, :, :30], K[:, :, :1]], dim=2))
+    with pytest.raises(ValueError):
+        DropKVCache(storage="ring")
