@@ -2,8 +2,8 @@
 // (and the same for V), a bit-exact copy.  Replaces dropkv_cache.py:479-491
 // (torch.gather along the sequence axis with the index expanded over D).
 //
-// Each thread moves one VW-byte chunk of one row of K and of V; consecutive
-// threads cover consecutive chunks of a row, so every warp reads and writes whole
+// Each thread moves VW-byte chunks of rows of K and of V; consecutive threads
+// cover consecutive chunks of a row, so every warp reads and writes whole
 // 128-byte lines.  Indices outside [0, Lk) produce zero rows (no trap).
 #include <algorithm>
 
@@ -12,12 +12,17 @@
 namespace dropkv {
 namespace {
 
+constexpr int GT_NT = 256;  // threads per block
+constexpr int GT_U = 2;     // chunks per thread and step: 2 K and 2 V loads in flight
+
 // in_sh / out_sh: vectors between consecutive heads of the input and the output.
+// Block x of row bh handles steps x, x + gridDim.x, ...; a step is GT_U * GT_NT
+// consecutive chunks, and all its index and data loads are issued before its stores.
 template <typename VT>
-__global__ void __launch_bounds__(256) gather_kernel(const VT* __restrict__ k, const VT* __restrict__ v,
-                                                     const int64_t* __restrict__ idx, int Lk, int keep_len,
-                                                     int CR, VT* __restrict__ ko, VT* __restrict__ vo,
-                                                     int64_t in_sh, int64_t out_sh) {
+__global__ void __launch_bounds__(GT_NT) gather_kernel(const VT* __restrict__ k, const VT* __restrict__ v,
+                                                       const int64_t* __restrict__ idx, int Lk, int keep_len,
+                                                       int CR, VT* __restrict__ ko, VT* __restrict__ vo,
+                                                       int64_t in_sh, int64_t out_sh) {
   const int bh = blockIdx.y;
   const int64_t n = (int64_t)keep_len * CR;
   const int64_t* ib = idx + (size_t)bh * keep_len;
@@ -25,21 +30,35 @@ __global__ void __launch_bounds__(256) gather_kernel(const VT* __restrict__ k, c
   const VT* vb = v + (size_t)bh * in_sh;
   VT* kob = ko + (size_t)bh * out_sh;
   VT* vob = vo + (size_t)bh * out_sh;
-  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < n;
-       c += (int64_t)gridDim.x * blockDim.x) {
-    int64_t i = c / CR;
-    int col = (int)(c - i * CR);
-    int64_t src = ib[i];
-    VT a, b;
-    if (src >= 0 && src < Lk) {
-      a = kb[src * CR + col];
-      b = vb[src * CR + col];
-    } else {
-      a = VT{};
-      b = VT{};
+  for (int64_t c0 = (int64_t)blockIdx.x * (GT_U * GT_NT) + threadIdx.x; c0 < n;
+       c0 += (int64_t)gridDim.x * (GT_U * GT_NT)) {
+    int64_t src[GT_U], i[GT_U];
+    int col[GT_U];
+#pragma unroll
+    for (int u = 0; u < GT_U; ++u) {
+      const int64_t c = c0 + u * GT_NT;
+      i[u] = c / CR;
+      col[u] = (int)(c - i[u] * CR);
+      src[u] = c < n ? ib[i[u]] : -1;
     }
-    kob[i * CR + col] = a;
-    vob[i * CR + col] = b;
+    VT a[GT_U], b[GT_U];
+#pragma unroll
+    for (int u = 0; u < GT_U; ++u) {
+      if (src[u] >= 0 && src[u] < Lk) {
+        a[u] = kb[src[u] * CR + col[u]];
+        b[u] = vb[src[u] * CR + col[u]];
+      } else {
+        a[u] = VT{};
+        b[u] = VT{};
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < GT_U; ++u) {
+      if (c0 + u * GT_NT < n) {
+        kob[i[u] * CR + col[u]] = a[u];
+        vob[i[u] * CR + col[u]] = b[u];
+      }
+    }
   }
 }
 
@@ -48,13 +67,20 @@ int launch_vec(const void* k, const void* v, int BH, int Lk, int row_bytes, cons
                int keep_len, void* ko, void* vo, cudaStream_t st, int64_t in_sh_bytes, int64_t out_sh_bytes) {
   int CR = row_bytes / (int)sizeof(VT);
   int64_t n = (int64_t)keep_len * CR;
-  int bx = (int)std::min<int64_t>((n + 255) / 256, 4096);
+  // one wave of blocks over the GPU (8 per SM), with the steps of a row spread
+  // evenly over its blocks
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t steps = (n + GT_U * GT_NT - 1) / (GT_U * GT_NT);
+  const int64_t target = std::max<int64_t>(1, (int64_t)sms * (2048 / GT_NT) / BH);
+  const int64_t per_block = (steps + target - 1) / target;
+  int bx = (int)std::min<int64_t>((steps + per_block - 1) / per_block, 65535);
   if (bx < 1) bx = 1;
   dim3 grid(bx, BH);
-  gather_kernel<VT><<<grid, 256, 0, st>>>(reinterpret_cast<const VT*>(k), reinterpret_cast<const VT*>(v),
-                                          idx, Lk, keep_len, CR, reinterpret_cast<VT*>(ko),
-                                          reinterpret_cast<VT*>(vo), in_sh_bytes / (int64_t)sizeof(VT),
-                                          out_sh_bytes / (int64_t)sizeof(VT));
+  gather_kernel<VT><<<grid, GT_NT, 0, st>>>(reinterpret_cast<const VT*>(k), reinterpret_cast<const VT*>(v),
+                                            idx, Lk, keep_len, CR, reinterpret_cast<VT*>(ko),
+                                            reinterpret_cast<VT*>(vo), in_sh_bytes / (int64_t)sizeof(VT),
+                                            out_sh_bytes / (int64_t)sizeof(VT));
   return check_launch("gather");
 }
 

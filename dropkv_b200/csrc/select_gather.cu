@@ -8,19 +8,22 @@
 //   1. pooled = sliding max over +-radius (halo read from global; van Herk /
 //      Gil-Werman blocks), the CTA's maximum is published;
 //   2. radix select of the keep_len-th largest order-preserving key (11/11/10-bit
-//      digits), two cluster barriers per digit: every CTA builds its histogram;
-//      CTA r sums bins [r*nb/CL, (r+1)*nb/CL) over the cluster (reduce-scatter);
+//      digits), one cluster barrier per digit: every CTA builds its histogram in
+//      its own shared memory and adds the non-zero bins into their owner's copy
+//      (CTA r owns bins [r*nb/CL, (r+1)*nb/CL), a separate array per digit, so
+//      no barrier is needed before the next digit's adds); after the barrier
 //      every CTA reads all reduced bins back and finds the selected bin itself.
 //      In the first digit the row maximum is formed from the published CTA
 //      maxima and the protected tail (value amax + 1, dropkv_cache.py:465-467)
-//      is counted by the owner of its bin; from then on protected positions carry
-//      that key;
+//      is added to its bin by every CTA on read-back; from then on protected
+//      positions carry that key;
 //   3. ordered compaction: warp-contiguous ranges with ballots give every kept
 //      position its rank; CTA totals of keys > T and == T are exchanged; the first
 //      (k - #{> T}) keys equal to T in index order are kept (ties to the lower
 //      index) and written to keep_idx in ascending order.
-// No wait here is unbounded: cluster barriers are hardware barriers of
-// co-scheduled CTAs.
+// One CTA of 1024 threads per SM: the clusters are placed one CTA per SM, so the
+// whole SM's warps go to the row. No wait here is unbounded: cluster barriers are
+// hardware barriers of co-scheduled CTAs.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -32,7 +35,7 @@ namespace cg = cooperative_groups;
 namespace dropkv {
 namespace {
 
-constexpr int SG_NT = 512;  // 16 warps
+constexpr int SG_NT = 1024;  // 32 warps
 constexpr int SG_NW = SG_NT / 32;
 constexpr int SG_MAXCL = 16;
 
@@ -64,8 +67,9 @@ __device__ __forceinline__ int sg_block_excl_scan(int v, int* tmp, int* total) {
   return res;
 }
 
-// Word offset of the reduced-bin array in the dynamic shared memory: after keys,
-// buf and hsuf, rounded up to 4 words (uint4 accesses).
+// Word offset of the reduced-bin arrays (one per digit, 2048 / CL words each) in the
+// dynamic shared memory: after keys, buf and hsuf, rounded up to 4 words (uint4
+// accesses).
 __host__ __device__ constexpr int sg_red_offset(int chunk, int radius) {
   return (chunk + 2 * (chunk + 2 * radius) + 3) & ~3;
 }
@@ -78,11 +82,23 @@ struct __align__(16) SgShared {  // static part of the shared memory
   float fmax_slot;      // this CTA's largest pooled value (read by the cluster)
   int cnt_slot[2];      // this CTA's (> T, == T) counts (read by the cluster)
   int sel[2];           // selected bin, remaining k
+  uint32_t kbig;        // key of the protected tail (amax + 1)
+  int ncand;            // keys left after the first digit (candidate list length)
+  int before[2];        // keys this CTA writes after (cluster prefix), ties kept here
 };
+
+// Cluster barrier split into its two halves: arrive publishes this thread's
+// earlier shared-memory writes to the cluster, wait makes the others' visible.
+__device__ __forceinline__ void sg_cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void sg_cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 // RT: the pooling radius when known at compile time (unrolled block loops), or -1.
 template <int RT>
-__global__ void __launch_bounds__(SG_NT, 2) cluster_select_kernel(const float* __restrict__ scores, int Lk,
+__global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* __restrict__ scores, int Lk,
                                                                   int chunk, int radius_rt, int protect,
                                                                   int keep_len, int64_t* __restrict__ keep_idx) {
   const int radius = RT >= 0 ? RT : radius_rt;
@@ -96,8 +112,12 @@ __global__ void __launch_bounds__(SG_NT, 2) cluster_select_kernel(const float* _
   uint32_t* keys = dyn;                                 // [chunk]
   float* buf = reinterpret_cast<float*>(dyn + chunk);   // [chunk + 2 radius]
   float* hsuf = buf + chunk + 2 * radius;               // [chunk + 2 radius]
-  // [2048 / CL] reduced bins, read as uint4: 16-byte aligned whatever chunk is
+  uint32_t* cand = reinterpret_cast<uint32_t*>(buf);    // candidate keys, once pooling is done
+  // [3][2048 / CL] reduced bins, read as uint4: 16-byte aligned whatever chunk is
   uint32_t* red = dyn + sg_red_offset(chunk, radius);
+  for (int i = tid; i < 3 * (2048 / CL); i += SG_NT) red[i] = 0;
+  if (tid == 0) S.ncand = 0;
+  sg_cluster_arrive();  // waited for before the first adds into another CTA's arrays
 
   const int j0 = min(Lk, r * chunk), j1 = min(Lk, j0 + chunk);
   const int n = j1 - j0;
@@ -187,64 +207,63 @@ __global__ void __launch_bounds__(SG_NT, 2) cluster_select_kernel(const float* _
     const int sh = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
     const int nb = pass == 2 ? 1024 : 2048;
     const uint32_t dmask = (uint32_t)(nb - 1);
+    const int per = nb / CL;  // bins per owner; CL is a power of two, so a multiple of 4
+    uint32_t* redp = red + pass * (2048 / CL);
     for (int i = tid; i < nb; i += SG_NT) S.hist[i] = 0;
     __syncthreads();
     // Pooled scores share few exponents, so the keys of a digit crowd into a few
     // bins: lanes with equal bins are combined (one atomic per bin and warp).
-    // The protected tail is left out of the first digit (its key is not known yet).
-    const int i_prot = (pass == 0) ? max(0, pstart - j0) : n;
-    for (int base = 0; base < n; base += SG_NT) {
+    // The protected tail is left out of the first digit (its key is not known yet);
+    // the later digits run over the candidate list, the keys that matched the first.
+    const uint32_t* src = pass == 0 ? keys : cand;
+    const int ns = pass == 0 ? n : S.ncand;
+    const int i_prot = (pass == 0) ? max(0, pstart - j0) : ns;
+    for (int base = 0; base < ns; base += SG_NT) {
       const int i = base + tid;
       uint32_t bin = 0xffffffffu;
-      if (i < n && i < i_prot) {
-        const uint32_t key = keys[i];
+      if (i < ns && i < i_prot) {
+        const uint32_t key = src[i];
         if ((key & pmask) == prefix) bin = (key >> sh) & dmask;
       }
       const uint32_t same = __match_any_sync(0xffffffffu, bin);
       if (bin != 0xffffffffu && lane == __ffs(same) - 1) atomicAdd(&S.hist[bin], (uint32_t)__popc(same));
     }
-    cluster.sync();  // histograms (and, before the first digit, CTA maxima) complete
-    uint32_t kbig = 0;
-    if (pass == 0) {
-      float amax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < SG_MAXCL; ++c)
-        if (c < CL) amax = fmaxf(amax, *cluster.map_shared_rank(&S.fmax_slot, c));
-      kbig = ordered_key(amax + 1.0f);
-    }
-    // reduce-scatter: this CTA owns bins [b_lo, b_lo + per), 4 per thread (CL is a
-    // power of two, so per = nb / CL is a multiple of 4); all loads independent
-    const int per = nb / CL;
-    const int b_lo = r * per;
-    if (tid * 4 < per) {
-      uint32_t c4[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-      for (int c = 0; c < SG_MAXCL; ++c) {
-        if (c < CL) {
-          const uint4 h4 = *reinterpret_cast<const uint4*>(cluster.map_shared_rank(S.hist, c) + b_lo + tid * 4);
-          c4[0] += h4.x;
-          c4[1] += h4.y;
-          c4[2] += h4.z;
-          c4[3] += h4.w;
-        }
+    __syncthreads();
+    if (pass == 0) sg_cluster_wait();  // every owner has cleared its arrays (arrive at the start)
+    for (int bin = tid; bin < nb; bin += SG_NT) {
+      const uint32_t c = S.hist[bin];
+      if (c) {
+        const int owner = bin / per;
+        atomicAdd(cluster.map_shared_rank(redp, owner) + (bin - owner * per), c);
       }
-      if (pass == 0 && protect > 0) {  // the whole protected tail shares one key
-        const int bb = (int)((kbig >> sh) & dmask) - (b_lo + tid * 4);
-        if (bb >= 0 && bb < 4) c4[bb] += (uint32_t)protect;
-      }
-      *reinterpret_cast<uint4*>(red + tid * 4) = make_uint4(c4[0], c4[1], c4[2], c4[3]);
     }
-    cluster.sync();  // reduced bins of every owner complete
+    sg_cluster_arrive();  // this CTA's adds (and, before the first digit, its maximum) are done
+    sg_cluster_wait();
+    if (pass == 0 && warp == 0) {  // row maximum from the CTA maxima; key of the protected tail
+      float m = lane < CL ? *cluster.map_shared_rank(&S.fmax_slot, lane) : -INFINITY;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) S.kbig = ordered_key(m + 1.0f);
+    }
     // every CTA reads all reduced bins (thread t: bins [4t, 4t + 4)) and finds the
     // bin holding the k-th largest key
     int cnt[4] = {0, 0, 0, 0};
     if (tid * 4 < nb) {
       const int b = tid * 4, owner = b / per;
-      const uint4 c4 = *reinterpret_cast<const uint4*>(cluster.map_shared_rank(red, owner) + (b - owner * per));
+      const uint4 c4 = *reinterpret_cast<const uint4*>(cluster.map_shared_rank(redp, owner) + (b - owner * per));
       cnt[0] = (int)c4.x;
       cnt[1] = (int)c4.y;
       cnt[2] = (int)c4.z;
       cnt[3] = (int)c4.w;
+    }
+    if (pass == 0) {
+      __syncthreads();
+      if (protect > 0) {  // the whole protected tail shares one key
+        const int bb = (int)((S.kbig >> sh) & dmask) - tid * 4;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (bb == u) cnt[u] += protect;
+      }
     }
     const int my_sum = cnt[0] + cnt[1] + cnt[2] + cnt[3];
     int total;
@@ -262,8 +281,33 @@ __global__ void __launch_bounds__(SG_NT, 2) cluster_select_kernel(const float* _
     prefix |= ((uint32_t)S.sel[0]) << sh;
     pmask |= dmask << sh;
     k = S.sel[1];
-    if (pass == 0)  // protected positions carry the key of amax + 1 from here on
-      for (int i = max(0, pstart - j0) + tid; i < n; i += SG_NT) keys[i] = kbig;
+    if (pass == 0) {
+      // protected positions carry the key of amax + 1 from here on; the keys that
+      // match the first digit go to the candidate list (in any order: the later
+      // digits only count them)
+      const uint32_t kbig = S.kbig;
+      const int ip0 = max(0, pstart - j0);
+      const uint32_t lt = (1u << lane) - 1u;
+      for (int base = 0; base < n; base += SG_NT) {
+        const int i = base + tid;
+        uint32_t key = 0;
+        if (i < n) {
+          key = keys[i];
+          if (i >= ip0) {
+            key = kbig;
+            keys[i] = kbig;
+          }
+        }
+        const bool c = i < n && (key & pmask) == prefix;
+        const uint32_t m = __ballot_sync(0xffffffffu, c);
+        if (m) {
+          int b0 = 0;
+          if (lane == 0) b0 = atomicAdd(&S.ncand, __popc(m));
+          b0 = __shfl_sync(0xffffffffu, b0, 0);
+          if (c) cand[b0 + __popc(m & lt)] = key;
+        }
+      }
+    }
     __syncthreads();
   }
   const uint32_t T = prefix;
@@ -294,22 +338,38 @@ __global__ void __launch_bounds__(SG_NT, 2) cluster_select_kernel(const float* _
     wbase = __shfl_sync(0xffffffffu, inc - v, warp);
     ctot = __shfl_sync(0xffffffffu, inc, 31);
   }
-  const int tot_gt = ctot & 0xffff, tot_eq = ctot >> 16;
   if (tid == 0) {
-    S.cnt_slot[0] = tot_gt;
-    S.cnt_slot[1] = tot_eq;
+    S.cnt_slot[0] = ctot & 0xffff;
+    S.cnt_slot[1] = ctot >> 16;
   }
-  cluster.sync();
-  int eq_before = 0, out_before = 0;
+  sg_cluster_arrive();
+  sg_cluster_wait();
+  if (warp == 0) {
+    // CTAs c < r come first: all their keys > T, and the first (need_eq - ties
+    // before c) of their ties
+    int g = 0, e = 0;
+    if (lane < r) {
+      const int* sl = cluster.map_shared_rank(S.cnt_slot, lane);
+      g = sl[0];
+      e = sl[1];
+    }
+    int einc = e;
 #pragma unroll
-  for (int c = 0; c < SG_MAXCL; ++c) {
-    if (c < r) {
-      const int* sl = cluster.map_shared_rank(S.cnt_slot, c);
-      const int g = sl[0], e = sl[1];
-      out_before += g + max(0, min(e, need_eq - eq_before));
-      eq_before += e;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, einc, o);
+      if (lane >= o) einc += t;
+    }
+    int term = (lane < r) ? g + max(0, min(e, need_eq - (einc - e))) : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) term += __shfl_xor_sync(0xffffffffu, term, o);
+    const int eq_all = __shfl_sync(0xffffffffu, einc, 31);
+    if (lane == 0) {
+      S.before[0] = term;
+      S.before[1] = eq_all;
     }
   }
+  __syncthreads();
+  const int out_before = S.before[0], eq_before = S.before[1];
   const int need_local = max(0, need_eq - eq_before);  // ties this CTA keeps, lowest index first
   int64_t* orow = keep_idx + (size_t)row * keep_len + out_before;
   int g = wbase & 0xffff, e = wbase >> 16;
@@ -334,17 +394,21 @@ __global__ void __launch_bounds__(SG_NT, 2) cluster_select_kernel(const float* _
 }  // namespace
 
 // Cluster size and chunk for a row of Lk positions; 0 if the row does not fit.
-// Up to 16 CTAs of <= 8192 positions, sized so that two CTAs share an SM and all
-// clusters of a typical launch are resident at once.
-static int sg_cluster_for(int Lk, int radius, int* chunk_out, size_t* smem_out) {
-  int cl = 1;
-  while (cl < SG_MAXCL && (Lk + cl - 1) / cl > 4096) cl *= 2;
+// The largest cluster considered gives each CTA <= 4096 positions (up to 16 CTAs);
+// a cluster of half that size is the other candidate (see launch_cluster_select).
+static int sg_chunk(int Lk, int radius, int cl, int* chunk_out, size_t* smem_out) {
   const int chunk = (Lk + cl - 1) / cl;
-  const size_t smem = ((size_t)sg_red_offset(chunk, radius) + 2048 / cl) * 4;
+  const size_t smem = ((size_t)sg_red_offset(chunk, radius) + 3 * (2048 / cl)) * 4;
   if (smem + sizeof(SgShared) > 227 * 1024) return 0;
   *chunk_out = chunk;
   *smem_out = smem;
   return cl;
+}
+
+static int sg_cluster_for(int Lk, int radius, int* chunk_out, size_t* smem_out) {
+  int cl = 1;
+  while (cl < SG_MAXCL && (Lk + cl - 1) / cl > 4096) cl *= 2;
+  return sg_chunk(Lk, radius, cl, chunk_out, smem_out);
 }
 
 bool select_gather_supported(int Lk, int kernel_size) {
@@ -353,27 +417,83 @@ bool select_gather_supported(int Lk, int kernel_size) {
   return sg_cluster_for(Lk, kernel_size / 2, &chunk, &smem) > 0;
 }
 
+using SgKernel = void (*)(const float*, int, int, int, int, int, int64_t*);
+
+// Clusters of `cl` CTAs that can be resident at once on this device (one CTA per
+// SM; a cluster must fit in one GPC, and GPCs differ in size), cached per device,
+// variant and cluster size for the shared-memory size last asked.
+static int sg_active_clusters(SgKernel kern, int variant, int cl, size_t smem) {
+  static int cache[2][5][64];
+  static size_t cache_smem[2][5][64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int lg = 0;
+  while ((1 << lg) < cl) ++lg;
+  if (dev < 64 && cache[variant][lg][dev] > 0 && cache_smem[variant][lg][dev] == smem) return cache[variant][lg][dev];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cl);
+  cfg.blockDim = dim3(SG_NT);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();  // clear the query's error; fall back to "all resident"
+    return 1 << 20;
+  }
+  if (dev < 64) {
+    cache_smem[variant][lg][dev] = smem;
+    cache[variant][lg][dev] = n;
+  }
+  return n;
+}
+
 static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
                                  int64_t* keep_idx, cudaStream_t st) {
+  const int radius = kernel_size / 2;
   int chunk;
   size_t smem;
-  const int cl = sg_cluster_for(Lk, kernel_size / 2, &chunk, &smem);
+  int cl = sg_cluster_for(Lk, radius, &chunk, &smem);
   if (!cl) return fail(DROPKV_ERR_UNSUPPORTED, "row of %d positions too long for the cluster select", Lk);
   // the default kernel_size 11 gets the unrolled pooling
-  const bool r5 = kernel_size / 2 == 5;
-  auto kern = r5 ? cluster_select_kernel<5> : cluster_select_kernel<-1>;
+  const bool r5 = radius == 5;
+  SgKernel kern = r5 ? cluster_select_kernel<5> : cluster_select_kernel<-1>;
   static unsigned long long attr_done[2] = {0, 0};  // per variant and device: attributes set for
   static size_t attr_smem[2][64] = {};              // the largest size used so far
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(attr_done[r5] & (1ull << dev)) || attr_smem[r5][dev] < smem) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %zu for the cluster select", smem);
+  int chunk2 = 0;
+  size_t smem2 = 0;
+  const int cl2 = cl > 1 ? sg_chunk(Lk, radius, cl / 2, &chunk2, &smem2) : 0;
+  const size_t smem_max = std::max(smem, smem2);
+  if (dev >= 64 || !(attr_done[r5] & (1ull << dev)) || attr_smem[r5][dev] < smem_max) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max) != cudaSuccess)
+      return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %zu for the cluster select", smem_max);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       return fail(DROPKV_ERR_CUDA, "cannot allow 16-CTA clusters for the cluster select");
     if (dev < 64) {
       attr_done[r5] |= (1ull << dev);
-      attr_smem[r5][dev] = smem;
+      attr_smem[r5][dev] = smem_max;
+    }
+  }
+  if (cl2) {
+    // Rows run one cluster each; rows beyond the resident clusters wait for a
+    // second wave. Estimated time per wave: a fixed ~6 us of barriers plus
+    // ~1.6 us per 1024 positions of a CTA's chunk (measured on B200).
+    auto cost = [&](int c, int ch, size_t sm) {
+      const int act = sg_active_clusters(kern, r5, c, sm);
+      const int waves = (BH + act - 1) / act;
+      return waves * (6.0 + 1.6 * ch / 1024.0);
+    };
+    if (cost(cl2, chunk2, smem2) < cost(cl, chunk, smem)) {
+      cl = cl2;
+      chunk = chunk2;
+      smem = smem2;
     }
   }
   cudaLaunchConfig_t cfg = {};
@@ -388,7 +508,7 @@ static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, scores, Lk, chunk, kernel_size / 2, protect, keep_len, keep_idx);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, scores, Lk, chunk, radius, protect, keep_len, keep_idx);
   if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "cluster select launch: %s", cudaGetErrorString(e));
   return check_launch("cluster_select");
 }

@@ -75,6 +75,15 @@ def test_select_large_row():
     assert (np.diff(got, axis=-1) > 0).all()
 
 
+@pytest.mark.parametrize("shape", [(1, 1, 131072), (1, 20, 40000), (4, 8, 8192), (2, 16, 65536)])
+def test_select_row_counts(shape):
+    # the launch picks the cluster size from the row count and the resident
+    # clusters; every choice must give the same kept set
+    g = torch.Generator().manual_seed(shape[1])
+    s = torch.rand(*shape, generator=g) ** 4  # crowded exponents, as pooled scores are
+    _check(s, 11, 8, shape[-1] // 7)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("D", [32, 64, 128, 256])
 def test_gather_bit_exact(dtype, D):
