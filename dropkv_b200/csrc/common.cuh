@@ -46,6 +46,16 @@ __device__ __forceinline__ uint32_t ordered_key(float f) {
   uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may be scheduled while its predecessor on the stream is still
+// running; pdl_wait() blocks until the predecessor has completed and its writes
+// are visible (a no-op when there is no such predecessor).
+// pdl_launch_dependents() lets the next kernel be scheduled from this point on.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float key_to_float(uint32_t k) {
   uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
   return __uint_as_float(u);

@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(GT_NT) gather_kernel(const VT* __restrict__ k,
   const VT* vb = v + (size_t)bh * in_sh;
   VT* kob = ko + (size_t)bh * out_sh;
   VT* vob = vo + (size_t)bh * out_sh;
+  pdl_wait();  // keep_idx may come from the kernel before this one
   for (int64_t c0 = (int64_t)blockIdx.x * (GT_U * GT_NT) + threadIdx.x; c0 < n;
        c0 += (int64_t)gridDim.x * (GT_U * GT_NT)) {
     int64_t src[GT_U], i[GT_U];
@@ -76,11 +77,20 @@ int launch_vec(const void* k, const void* v, int BH, int Lk, int row_bytes, cons
   const int64_t per_block = (steps + target - 1) / target;
   int bx = (int)std::min<int64_t>((steps + per_block - 1) / per_block, 65535);
   if (bx < 1) bx = 1;
-  dim3 grid(bx, BH);
-  gather_kernel<VT><<<grid, GT_NT, 0, st>>>(reinterpret_cast<const VT*>(k), reinterpret_cast<const VT*>(v),
-                                            idx, Lk, keep_len, CR, reinterpret_cast<VT*>(ko),
-                                            reinterpret_cast<VT*>(vo), in_sh_bytes / (int64_t)sizeof(VT),
-                                            out_sh_bytes / (int64_t)sizeof(VT));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(bx, BH);
+  cfg.blockDim = dim3(GT_NT);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // may start as the selection ends
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gather_kernel<VT>, reinterpret_cast<const VT*>(k),
+                                     reinterpret_cast<const VT*>(v), idx, Lk, keep_len, CR,
+                                     reinterpret_cast<VT*>(ko), reinterpret_cast<VT*>(vo),
+                                     in_sh_bytes / (int64_t)sizeof(VT), out_sh_bytes / (int64_t)sizeof(VT));
+  if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "gather launch: %s", cudaGetErrorString(e));
   return check_launch("gather");
 }
 

@@ -319,6 +319,9 @@ __global__ void __launch_bounds__(NTH, 1)
   static_assert(TMAX <= kMaxTiles, "s_done barriers");
   static_assert(HC >= 4 && HC <= 16, "column split");
   extern __shared__ uint8_t raw[];
+  // the selection launched after this kernel may be scheduled as SMs free up; it
+  // waits for this grid's completion before reading the scores
+  pdl_launch_dependents();
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::BAR);
   uint64_t* freeb = full + NS;

@@ -121,6 +121,8 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
 
   const int j0 = min(Lk, r * chunk), j1 = min(Lk, j0 + chunk);
   const int n = j1 - j0;
+  pdl_wait();               // the scores come from the kernel before this one
+  pdl_launch_dependents();  // the gather may be scheduled on the SMs left free
   const float* srow = scores + (size_t)row * Lk;
   const int pstart = Lk - protect;
 
@@ -179,6 +181,7 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
   }
   __syncthreads();
   float lmax = -INFINITY;
+#pragma unroll 4
   for (int i = tid; i < n; i += SG_NT) {
     const int x = j0 + i - h0;
     const int lo = max(0, x - radius), hi = min(H - 1, x + radius);
@@ -211,13 +214,15 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
     uint32_t* redp = red + pass * (2048 / CL);
     for (int i = tid; i < nb; i += SG_NT) S.hist[i] = 0;
     __syncthreads();
-    // Pooled scores share few exponents, so the keys of a digit crowd into a few
-    // bins: lanes with equal bins are combined (one atomic per bin and warp).
+    // Pooled scores form plateaus and share few exponents, so neighbouring lanes
+    // mostly fall into the same bin: each run of equal bins in a warp is added by
+    // its first lane (one atomic per run).
     // The protected tail is left out of the first digit (its key is not known yet);
     // the later digits run over the candidate list, the keys that matched the first.
     const uint32_t* src = pass == 0 ? keys : cand;
     const int ns = pass == 0 ? n : S.ncand;
     const int i_prot = (pass == 0) ? max(0, pstart - j0) : ns;
+#pragma unroll 4
     for (int base = 0; base < ns; base += SG_NT) {
       const int i = base + tid;
       uint32_t bin = 0xffffffffu;
@@ -225,8 +230,14 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
         const uint32_t key = src[i];
         if ((key & pmask) == prefix) bin = (key >> sh) & dmask;
       }
-      const uint32_t same = __match_any_sync(0xffffffffu, bin);
-      if (bin != 0xffffffffu && lane == __ffs(same) - 1) atomicAdd(&S.hist[bin], (uint32_t)__popc(same));
+      const uint32_t prev = __shfl_up_sync(0xffffffffu, bin, 1);
+      const bool starts = lane == 0 || prev != bin;
+      const uint32_t heads = __ballot_sync(0xffffffffu, starts);
+      if (starts && bin != 0xffffffffu) {
+        const uint32_t after = heads & ~((2u << lane) - 1u);  // run starts past this lane
+        const int end = after ? __ffs(after) - 1 : 32;
+        atomicAdd(&S.hist[bin], (uint32_t)(end - lane));
+      }
     }
     __syncthreads();
     if (pass == 0) sg_cluster_wait();  // every owner has cleared its arrays (arrive at the start)
@@ -288,6 +299,7 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
       const uint32_t kbig = S.kbig;
       const int ip0 = max(0, pstart - j0);
       const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll 4
       for (int base = 0; base < n; base += SG_NT) {
         const int i = base + tid;
         uint32_t key = 0;
@@ -318,6 +330,7 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
   const int segw = ((n + SG_NT - 1) / SG_NT) * 32;
   const int w0 = min(n, warp * segw), w1 = min(n, w0 + segw);
   int cgt = 0, ceq = 0;
+#pragma unroll 4
   for (int base = w0; base < w1; base += 32) {
     const int i = base + lane;
     const uint32_t key = (i < w1) ? keys[i] : 0u;
@@ -374,6 +387,7 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
   int64_t* orow = keep_idx + (size_t)row * keep_len + out_before;
   int g = wbase & 0xffff, e = wbase >> 16;
   const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll 4
   for (int base = w0; base < w1; base += 32) {
     const int i = base + lane;
     const uint32_t key = (i < w1) ? keys[i] : 0u;
@@ -501,13 +515,15 @@ static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel
   cfg.blockDim = dim3(SG_NT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cl;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, scores, Lk, chunk, radius, protect, keep_len, keep_idx);
   if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "cluster select launch: %s", cudaGetErrorString(e));
   return check_launch("cluster_select");
