@@ -3,10 +3,12 @@
 // copied by the gather kernel, which spreads over the whole GPU.
 //
 // One thread-block cluster of CL CTAs per (sequence, KV head) row; CTA r of the
-// cluster owns positions [r*chunk, (r+1)*chunk) and keeps them in shared memory.
+// cluster owns positions [r*chunk, (r+1)*chunk); each of its threads owns a run of
+// consecutive positions and keeps their keys in registers for the whole kernel.
 // The cluster cooperates through distributed shared memory:
-//   1. pooled = sliding max over +-radius (halo read from global; van Herk /
-//      Gil-Werman blocks), the CTA's maximum is published;
+//   1. pooled = sliding max over +-radius (the score window with its halo staged
+//      in shared memory; max by doubling spans in registers), the CTA's maximum
+//      is published;
 //   2. radix select of the keep_len-th largest order-preserving key (11/11/10-bit
 //      digits), one cluster barrier per digit: every CTA builds its histogram in
 //      its own shared memory and adds the non-zero bins into their owner's copy
@@ -16,9 +18,10 @@
 //      In the first digit the row maximum is formed from the published CTA
 //      maxima and the protected tail (value amax + 1, dropkv_cache.py:465-467)
 //      is added to its bin by every CTA on read-back; from then on protected
-//      positions carry that key;
-//   3. ordered compaction: warp-contiguous ranges with ballots give every kept
-//      position its rank; CTA totals of keys > T and == T are exchanged; the first
+//      positions carry that key. The keys matching the first digit form a
+//      candidate list that the later digits scan instead of the whole chunk;
+//   3. ordered compaction: one block scan of the per-thread counts of keys > T
+//      and == T ranks every position; CTA totals are exchanged; the first
 //      (k - #{> T}) keys equal to T in index order are kept (ties to the lower
 //      index) and written to keep_idx in ascending order.
 // One CTA of 1024 threads per SM: the clusters are placed one CTA per SM, so the
@@ -67,17 +70,22 @@ __device__ __forceinline__ int sg_block_excl_scan(int v, int* tmp, int* total) {
   return res;
 }
 
+// Each thread owns KPT consecutive positions of its CTA's chunk (a chunk holds at
+// most SG_NT * KPT positions) and keeps their keys in registers. The score window
+// is staged in shared memory with one padding word after every KPT words, so that
+// a warp reading its lanes' runs of consecutive positions hits distinct banks.
+__host__ __device__ constexpr int sg_pad(int q, int kpt) { return q + q / kpt; }
+
 // Word offset of the reduced-bin arrays (one per digit, 2048 / CL words each) in the
-// dynamic shared memory: after keys, buf and hsuf, rounded up to 4 words (uint4
-// accesses).
-__host__ __device__ constexpr int sg_red_offset(int chunk, int radius) {
-  return (chunk + 2 * (chunk + 2 * radius) + 3) & ~3;
+// dynamic shared memory: after the padded score window, rounded up to 4 words
+// (uint4 accesses).
+__host__ __device__ constexpr int sg_red_offset(int chunk, int radius, int kpt) {
+  return (sg_pad(chunk + 2 * radius, kpt) + 1 + 3) & ~3;
 }
 
 struct __align__(16) SgShared {  // static part of the shared memory
   uint32_t hist[2048];  // this CTA's histogram of the current digit
   int itmp[33];
-  int wcnt[SG_NW];      // per-warp packed (> T, == T) counts
   float ftmp[SG_NW];
   float fmax_slot;      // this CTA's largest pooled value (read by the cluster)
   int cnt_slot[2];      // this CTA's (> T, == T) counts (read by the cluster)
@@ -96,8 +104,9 @@ __device__ __forceinline__ void sg_cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// RT: the pooling radius when known at compile time (unrolled block loops), or -1.
-template <int RT>
+// RT: the pooling radius when known at compile time (pooling in registers), or -1.
+// KPT: positions per thread (4, 8 or 16).
+template <int RT, int KPT>
 __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* __restrict__ scores, int Lk,
                                                                   int chunk, int radius_rt, int protect,
                                                                   int keep_len, int64_t* __restrict__ keep_idx) {
@@ -109,12 +118,10 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __shared__ SgShared S;
   extern __shared__ uint32_t dyn[];
-  uint32_t* keys = dyn;                                 // [chunk]
-  float* buf = reinterpret_cast<float*>(dyn + chunk);   // [chunk + 2 radius]
-  float* hsuf = buf + chunk + 2 * radius;               // [chunk + 2 radius]
-  uint32_t* cand = reinterpret_cast<uint32_t*>(buf);    // candidate keys, once pooling is done
+  float* buf = reinterpret_cast<float*>(dyn);  // padded window of positions [j0 - radius, j1 + radius)
+  uint32_t* cand = dyn;                        // candidate keys, once the keys are in registers
   // [3][2048 / CL] reduced bins, read as uint4: 16-byte aligned whatever chunk is
-  uint32_t* red = dyn + sg_red_offset(chunk, radius);
+  uint32_t* red = dyn + sg_red_offset(chunk, radius, KPT);
   for (int i = tid; i < 3 * (2048 / CL); i += SG_NT) red[i] = 0;
   if (tid == 0) S.ncand = 0;
   sg_cluster_arrive();  // waited for before the first adds into another CTA's arrays
@@ -127,70 +134,66 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
   const int pstart = Lk - protect;
 
   // ---- 1. sliding max --------------------------------------------------------
-  const int h0 = max(0, j0 - radius), h1 = min(Lk, j1 + radius);
-  const int H = h1 - h0;
-  for (int j = h0 + tid; j < h1; j += 8 * SG_NT) {  // 8 independent loads in flight per thread
+  // window index q <-> row position j0 - radius + q; -inf outside the row, as
+  // max_pool1d pads
+  const int Q = n + 2 * radius;
+  const int jb = j0 - radius;
+  for (int q = tid; q < Q; q += 8 * SG_NT) {  // 8 independent loads in flight per thread
     float v8[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const int jj = j + u * SG_NT;
-      v8[u] = (jj < h1) ? __ldg(srow + jj) : 0.f;
+      const int qq = q + u * SG_NT, j = jb + qq;
+      v8[u] = (qq < Q && j >= 0 && j < Lk) ? __ldg(srow + j) : -INFINITY;
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const int jj = j + u * SG_NT;
-      if (jj < h1) buf[jj - h0] = v8[u];
+      const int qq = q + u * SG_NT;
+      if (qq < Q) buf[sg_pad(qq, KPT)] = v8[u];
     }
   }
   __syncthreads();
-  // max over [x - radius, x + radius] clipped to the row: blocks of w = 2 radius + 1
-  // positions; hsuf = suffix max inside the block, then buf becomes the prefix max
-  // inside the block (in place)
-  const int wlen = 2 * radius + 1;
-  for (int b = tid; b * wlen < H; b += SG_NT) {
-    const int s0 = b * wlen, s1 = min(H, s0 + wlen);
-    if (RT >= 0 && s1 - s0 == 2 * RT + 1) {  // whole block, unrolled: all loads issued together
-      constexpr int WL = 2 * (RT > 0 ? RT : 0) + 1;
-      float v[WL];
+  // this thread: chunk positions x0 + u, u < nv
+  const int x0 = KPT * tid;
+  const int nv = max(0, min(KPT, n - x0));
+  float pooled[KPT];
+  if (RT >= 0) {
+    constexpr int R = RT >= 0 ? RT : 0;
+    constexpr int W = 2 * R + 1;
+    constexpr int WN = KPT + 2 * R;
+    constexpr int P = W >= 16 ? 16 : (W >= 8 ? 8 : (W >= 4 ? 4 : (W >= 2 ? 2 : 1)));
+    static_assert(W <= 2 * P, "window covered by two spans");
+    float v[WN];
 #pragma unroll
-      for (int t = 0; t < WL; ++t) v[t] = buf[s0 + t];
+    for (int i = 0; i < WN; ++i) {
+      const int q = x0 + i;
+      v[i] = q < Q ? buf[sg_pad(q, KPT)] : -INFINITY;
+    }
+    // doubling in place: after the step of span sp, v[i] = max of the inputs [i, i + 2 sp)
+#pragma unroll
+    for (int sp = 1; sp < P; sp *= 2) {
+#pragma unroll
+      for (int i = 0; i + sp < WN; ++i) v[i] = fmaxf(v[i], v[i + sp]);
+    }
+    // [u, u + W) = [u, u + P) U [u + W - P, u + W)
+#pragma unroll
+    for (int u = 0; u < KPT; ++u) pooled[u] = fmaxf(v[u], v[u + W - P]);
+  } else {
+#pragma unroll
+    for (int u = 0; u < KPT; ++u) {
       float m = -INFINITY;
-#pragma unroll
-      for (int t = WL - 1; t >= 0; --t) {
-        m = fmaxf(m, v[t]);
-        hsuf[s0 + t] = m;
+      for (int i = 0; i <= 2 * radius; ++i) {
+        const int q = x0 + u + i;
+        if (q < Q) m = fmaxf(m, buf[sg_pad(q, KPT)]);
       }
-      m = -INFINITY;
-#pragma unroll
-      for (int t = 0; t < WL; ++t) {
-        m = fmaxf(m, v[t]);
-        buf[s0 + t] = m;
-      }
-    } else {
-      float m = -INFINITY;
-      for (int x = s1 - 1; x >= s0; --x) {
-        m = fmaxf(m, buf[x]);
-        hsuf[x] = m;
-      }
-      m = -INFINITY;
-      for (int x = s0; x < s1; ++x) {
-        m = fmaxf(m, buf[x]);
-        buf[x] = m;
-      }
+      pooled[u] = m;
     }
   }
-  __syncthreads();
+  uint32_t key[KPT];
   float lmax = -INFINITY;
-#pragma unroll 4
-  for (int i = tid; i < n; i += SG_NT) {
-    const int x = j0 + i - h0;
-    const int lo = max(0, x - radius), hi = min(H - 1, x + radius);
-    const int blo = lo / wlen, bhi = hi / wlen;
-    // a window spans two blocks, or sits in one block clipped at the row's start
-    // (lo is a block start) or end (hi is the last position)
-    const float m = (blo != bhi) ? fmaxf(hsuf[lo], buf[hi]) : (lo == blo * wlen ? buf[hi] : hsuf[lo]);
-    keys[i] = ordered_key(m);
-    lmax = fmaxf(lmax, m);
+#pragma unroll
+  for (int u = 0; u < KPT; ++u) {
+    key[u] = ordered_key(pooled[u]);
+    if (u < nv) lmax = fmaxf(lmax, pooled[u]);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
@@ -201,6 +204,7 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
     for (int w = 1; w < SG_NW; ++w) m = fmaxf(m, S.ftmp[w]);
     S.fmax_slot = m;
   }
+  const int ip = pstart - j0 - x0;  // this thread's first protected position (may be <= 0 or >= KPT)
 
   // ---- 2. radix select over the cluster -------------------------------------
   uint32_t prefix = 0, pmask = 0;
@@ -214,29 +218,43 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
     uint32_t* redp = red + pass * (2048 / CL);
     for (int i = tid; i < nb; i += SG_NT) S.hist[i] = 0;
     __syncthreads();
-    // Pooled scores form plateaus and share few exponents, so neighbouring lanes
-    // mostly fall into the same bin: each run of equal bins in a warp is added by
-    // its first lane (one atomic per run).
-    // The protected tail is left out of the first digit (its key is not known yet);
-    // the later digits run over the candidate list, the keys that matched the first.
-    const uint32_t* src = pass == 0 ? keys : cand;
-    const int ns = pass == 0 ? n : S.ncand;
-    const int i_prot = (pass == 0) ? max(0, pstart - j0) : ns;
-#pragma unroll 4
-    for (int base = 0; base < ns; base += SG_NT) {
-      const int i = base + tid;
-      uint32_t bin = 0xffffffffu;
-      if (i < ns && i < i_prot) {
-        const uint32_t key = src[i];
-        if ((key & pmask) == prefix) bin = (key >> sh) & dmask;
+    // Pooled scores form plateaus and share few exponents, so neighbouring
+    // positions mostly fall into the same bin: each run of equal bins is added
+    // once. The protected tail is left out of the first digit (its key is not
+    // known yet); the later digits run over the candidate list, the keys that
+    // matched the first digit.
+    if (pass == 0) {
+      uint32_t cur = 0xffffffffu, run = 0;
+#pragma unroll
+      for (int u = 0; u < KPT; ++u) {
+        const uint32_t b = (u < nv && u < ip) ? (key[u] >> 21) : 0xffffffffu;
+        if (b != cur) {
+          if (cur != 0xffffffffu) atomicAdd(&S.hist[cur], run);
+          cur = b;
+          run = 1;
+        } else {
+          ++run;
+        }
       }
-      const uint32_t prev = __shfl_up_sync(0xffffffffu, bin, 1);
-      const bool starts = lane == 0 || prev != bin;
-      const uint32_t heads = __ballot_sync(0xffffffffu, starts);
-      if (starts && bin != 0xffffffffu) {
-        const uint32_t after = heads & ~((2u << lane) - 1u);  // run starts past this lane
-        const int end = after ? __ffs(after) - 1 : 32;
-        atomicAdd(&S.hist[bin], (uint32_t)(end - lane));
+      if (cur != 0xffffffffu) atomicAdd(&S.hist[cur], run);
+    } else {
+      const int ns = S.ncand;
+#pragma unroll 4
+      for (int base = 0; base < ns; base += SG_NT) {
+        const int i = base + tid;
+        uint32_t bin = 0xffffffffu;
+        if (i < ns) {
+          const uint32_t kk = cand[i];
+          if ((kk & pmask) == prefix) bin = (kk >> sh) & dmask;
+        }
+        const uint32_t prev = __shfl_up_sync(0xffffffffu, bin, 1);
+        const bool starts = lane == 0 || prev != bin;
+        const uint32_t heads = __ballot_sync(0xffffffffu, starts);
+        if (starts && bin != 0xffffffffu) {
+          const uint32_t after = heads & ~((2u << lane) - 1u);  // run starts past this lane
+          const int end = after ? __ffs(after) - 1 : 32;
+          atomicAdd(&S.hist[bin], (uint32_t)(end - lane));
+        }
       }
     }
     __syncthreads();
@@ -297,28 +315,24 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
       // match the first digit go to the candidate list (in any order: the later
       // digits only count them)
       const uint32_t kbig = S.kbig;
-      const int ip0 = max(0, pstart - j0);
-      const uint32_t lt = (1u << lane) - 1u;
-#pragma unroll 4
-      for (int base = 0; base < n; base += SG_NT) {
-        const int i = base + tid;
-        uint32_t key = 0;
-        if (i < n) {
-          key = keys[i];
-          if (i >= ip0) {
-            key = kbig;
-            keys[i] = kbig;
-          }
-        }
-        const bool c = i < n && (key & pmask) == prefix;
-        const uint32_t m = __ballot_sync(0xffffffffu, c);
-        if (m) {
-          int b0 = 0;
-          if (lane == 0) b0 = atomicAdd(&S.ncand, __popc(m));
-          b0 = __shfl_sync(0xffffffffu, b0, 0);
-          if (c) cand[b0 + __popc(m & lt)] = key;
-        }
+      int c = 0;
+#pragma unroll
+      for (int u = 0; u < KPT; ++u) {
+        if (u >= ip) key[u] = kbig;
+        c += (u < nv && (key[u] & pmask) == prefix) ? 1 : 0;
       }
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+      }
+      int base = 0;
+      if (lane == 31 && inc > 0) base = atomicAdd(&S.ncand, inc);
+      int pos = __shfl_sync(0xffffffffu, base, 31) + inc - c;
+#pragma unroll
+      for (int u = 0; u < KPT; ++u)
+        if (u < nv && (key[u] & pmask) == prefix) cand[pos++] = key[u];
     }
     __syncthreads();
   }
@@ -326,31 +340,19 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
   const int need_eq = k;
 
   // ---- 3. ordered compaction -------------------------------------------------
-  // Warp w owns positions [w*segw, (w+1)*segw), 32 consecutive ones per step.
-  const int segw = ((n + SG_NT - 1) / SG_NT) * 32;
-  const int w0 = min(n, warp * segw), w1 = min(n, w0 + segw);
+  // Kept: every key > T and the first need_eq keys == T in position order (ties to
+  // the lower index). Threads own consecutive positions, so one block scan of the
+  // packed (> T, == T) counts ranks every position of the CTA.
   int cgt = 0, ceq = 0;
-#pragma unroll 4
-  for (int base = w0; base < w1; base += 32) {
-    const int i = base + lane;
-    const uint32_t key = (i < w1) ? keys[i] : 0u;
-    cgt += __popc(__ballot_sync(0xffffffffu, i < w1 && key > T));
-    ceq += __popc(__ballot_sync(0xffffffffu, i < w1 && key == T));
-  }
-  if (lane == 0) S.wcnt[warp] = cgt | (ceq << 16);  // counts < 2^16
-  __syncthreads();
-  int wbase = 0, ctot = 0;  // packed counts of the warps before mine, and of the CTA
-  {
-    const int v = lane < SG_NW ? S.wcnt[lane] : 0;
-    int inc = v;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += t;
+  for (int u = 0; u < KPT; ++u) {
+    if (u < nv) {
+      cgt += key[u] > T ? 1 : 0;
+      ceq += key[u] == T ? 1 : 0;
     }
-    wbase = __shfl_sync(0xffffffffu, inc - v, warp);
-    ctot = __shfl_sync(0xffffffffu, inc, 31);
   }
+  int ctot;
+  const int cpre = sg_block_excl_scan(cgt | (ceq << 16), S.itmp, &ctot);  // counts < 2^16
   if (tid == 0) {
     S.cnt_slot[0] = ctot & 0xffff;
     S.cnt_slot[1] = ctot >> 16;
@@ -385,22 +387,19 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
   const int out_before = S.before[0], eq_before = S.before[1];
   const int need_local = max(0, need_eq - eq_before);  // ties this CTA keeps, lowest index first
   int64_t* orow = keep_idx + (size_t)row * keep_len + out_before;
-  int g = wbase & 0xffff, e = wbase >> 16;
-  const uint32_t lt = (1u << lane) - 1u;
-#pragma unroll 4
-  for (int base = w0; base < w1; base += 32) {
-    const int i = base + lane;
-    const uint32_t key = (i < w1) ? keys[i] : 0u;
-    const uint32_t gtm = __ballot_sync(0xffffffffu, i < w1 && key > T);
-    const uint32_t eqm = __ballot_sync(0xffffffffu, i < w1 && key == T);
-    const int eqb = e + __popc(eqm & lt);
-    const bool kept = (gtm >> lane & 1u) || ((eqm >> lane & 1u) && eqb < need_local);
-    if (kept) {
-      const int pos = g + __popc(gtm & lt) + min(eqb, need_local);
-      if (out_before + pos < keep_len) orow[pos] = j0 + i;
+  int g = cpre & 0xffff, e = cpre >> 16;
+  const int jx = j0 + x0;
+#pragma unroll
+  for (int u = 0; u < KPT; ++u) {
+    if (u < nv) {
+      const bool gt = key[u] > T, eq = key[u] == T;
+      if (gt || (eq && e < need_local)) {
+        const int pos = g + min(e, need_local);
+        if (out_before + pos < keep_len) orow[pos] = jx + u;
+      }
+      g += gt ? 1 : 0;
+      e += eq ? 1 : 0;
     }
-    g += __popc(gtm);
-    e += __popc(eqm);
   }
   cluster.sync();  // keep this CTA's shared memory alive until the cluster has read it
 }
@@ -410,9 +409,12 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
 // Cluster size and chunk for a row of Lk positions; 0 if the row does not fit.
 // The largest cluster considered gives each CTA <= 4096 positions (up to 16 CTAs);
 // a cluster of half that size is the other candidate (see launch_cluster_select).
+static int sg_kpt(int chunk) { return chunk <= 4 * SG_NT ? 4 : (chunk <= 8 * SG_NT ? 8 : 16); }
+
 static int sg_chunk(int Lk, int radius, int cl, int* chunk_out, size_t* smem_out) {
   const int chunk = (Lk + cl - 1) / cl;
-  const size_t smem = ((size_t)sg_red_offset(chunk, radius) + 3 * (2048 / cl)) * 4;
+  if (chunk > 16 * SG_NT) return 0;
+  const size_t smem = ((size_t)sg_red_offset(chunk, radius, sg_kpt(chunk)) + 3 * (2048 / cl)) * 4;
   if (smem + sizeof(SgShared) > 227 * 1024) return 0;
   *chunk_out = chunk;
   *smem_out = smem;
@@ -432,13 +434,42 @@ bool select_gather_supported(int Lk, int kernel_size) {
 }
 
 using SgKernel = void (*)(const float*, int, int, int, int, int, int64_t*);
+constexpr int SG_VARIANTS = 6;
+
+// kernel for the radius (5: the default kernel_size 11) and positions per thread
+static SgKernel sg_kernel(bool r5, int kpt, int* variant) {
+  static const SgKernel table[SG_VARIANTS] = {
+      cluster_select_kernel<-1, 4>, cluster_select_kernel<-1, 8>, cluster_select_kernel<-1, 16>,
+      cluster_select_kernel<5, 4>,  cluster_select_kernel<5, 8>,  cluster_select_kernel<5, 16>};
+  *variant = (r5 ? 3 : 0) + (kpt == 4 ? 0 : (kpt == 8 ? 1 : 2));
+  return table[*variant];
+}
+
+// Function attributes (dynamic shared memory, 16-CTA clusters), set once per device
+// and variant for the largest size used so far.
+static int sg_prepare(SgKernel kern, int variant, size_t smem) {
+  static unsigned long long done[SG_VARIANTS] = {};
+  static size_t done_smem[SG_VARIANTS][64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && (done[variant] & (1ull << dev)) && done_smem[variant][dev] >= smem) return DROPKV_OK;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %zu for the cluster select", smem);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    return fail(DROPKV_ERR_CUDA, "cannot allow 16-CTA clusters for the cluster select");
+  if (dev < 64) {
+    done[variant] |= (1ull << dev);
+    done_smem[variant][dev] = smem;
+  }
+  return DROPKV_OK;
+}
 
 // Clusters of `cl` CTAs that can be resident at once on this device (one CTA per
 // SM; a cluster must fit in one GPC, and GPCs differ in size), cached per device,
 // variant and cluster size for the shared-memory size last asked.
 static int sg_active_clusters(SgKernel kern, int variant, int cl, size_t smem) {
-  static int cache[2][5][64];
-  static size_t cache_smem[2][5][64];
+  static int cache[SG_VARIANTS][5][64];
+  static size_t cache_smem[SG_VARIANTS][5][64];
   int dev = 0;
   cudaGetDevice(&dev);
   int lg = 0;
@@ -457,7 +488,7 @@ static int sg_active_clusters(SgKernel kern, int variant, int cl, size_t smem) {
   cfg.numAttrs = 1;
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
-    cudaGetLastError();  // clear the query's error; fall back to "all resident"
+    cudaGetLastError();  // clear the query's error; assume every cluster is resident
     return 1 << 20;
   }
   if (dev < 64) {
@@ -470,44 +501,34 @@ static int sg_active_clusters(SgKernel kern, int variant, int cl, size_t smem) {
 static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
                                  int64_t* keep_idx, cudaStream_t st) {
   const int radius = kernel_size / 2;
+  const bool r5 = radius == 5;
   int chunk;
   size_t smem;
   int cl = sg_cluster_for(Lk, radius, &chunk, &smem);
   if (!cl) return fail(DROPKV_ERR_UNSUPPORTED, "row of %d positions too long for the cluster select", Lk);
-  // the default kernel_size 11 gets the unrolled pooling
-  const bool r5 = radius == 5;
-  SgKernel kern = r5 ? cluster_select_kernel<5> : cluster_select_kernel<-1>;
-  static unsigned long long attr_done[2] = {0, 0};  // per variant and device: attributes set for
-  static size_t attr_smem[2][64] = {};              // the largest size used so far
-  int dev = 0;
-  cudaGetDevice(&dev);
+  int variant;
+  SgKernel kern = sg_kernel(r5, sg_kpt(chunk), &variant);
+  int rc = sg_prepare(kern, variant, smem);
+  if (rc) return rc;
   int chunk2 = 0;
   size_t smem2 = 0;
-  const int cl2 = cl > 1 ? sg_chunk(Lk, radius, cl / 2, &chunk2, &smem2) : 0;
-  const size_t smem_max = std::max(smem, smem2);
-  if (dev >= 64 || !(attr_done[r5] & (1ull << dev)) || attr_smem[r5][dev] < smem_max) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max) != cudaSuccess)
-      return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %zu for the cluster select", smem_max);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-      return fail(DROPKV_ERR_CUDA, "cannot allow 16-CTA clusters for the cluster select");
-    if (dev < 64) {
-      attr_done[r5] |= (1ull << dev);
-      attr_smem[r5][dev] = smem_max;
-    }
-  }
-  if (cl2) {
+  if (cl > 1 && sg_chunk(Lk, radius, cl / 2, &chunk2, &smem2)) {
     // Rows run one cluster each; rows beyond the resident clusters wait for a
     // second wave. Estimated time per wave: a fixed ~6 us of barriers plus
     // ~1.6 us per 1024 positions of a CTA's chunk (measured on B200).
-    auto cost = [&](int c, int ch, size_t sm) {
-      const int act = sg_active_clusters(kern, r5, c, sm);
+    int variant2;
+    SgKernel kern2 = sg_kernel(r5, sg_kpt(chunk2), &variant2);
+    if ((rc = sg_prepare(kern2, variant2, smem2))) return rc;
+    auto cost = [&](SgKernel kr, int var, int c, int ch, size_t sm) {
+      const int act = sg_active_clusters(kr, var, c, sm);
       const int waves = (BH + act - 1) / act;
       return waves * (6.0 + 1.6 * ch / 1024.0);
     };
-    if (cost(cl2, chunk2, smem2) < cost(cl, chunk, smem)) {
-      cl = cl2;
+    if (cost(kern2, variant2, cl / 2, chunk2, smem2) < cost(kern, variant, cl, chunk, smem)) {
+      cl /= 2;
       chunk = chunk2;
       smem = smem2;
+      kern = kern2;
     }
   }
   cudaLaunchConfig_t cfg = {};
