@@ -24,9 +24,9 @@
 //      and == T ranks every position; CTA totals are exchanged; the first
 //      (k - #{> T}) keys equal to T in index order are kept (ties to the lower
 //      index) and written to keep_idx in ascending order.
-// One CTA of 1024 threads per SM: the clusters are placed one CTA per SM, so the
-// whole SM's warps go to the row. No wait here is unbounded: cluster barriers are
-// hardware barriers of co-scheduled CTAs.
+// CTAs of 512 threads: with up to 16 positions per thread two of them fit on an
+// SM, so launches with many rows keep all their clusters resident. No wait here is
+// unbounded: cluster barriers are hardware barriers of co-scheduled CTAs.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -38,7 +38,7 @@ namespace cg = cooperative_groups;
 namespace dropkv {
 namespace {
 
-constexpr int SG_NT = 1024;  // 32 warps
+constexpr int SG_NT = 512;  // 16 warps
 constexpr int SG_NW = SG_NT / 32;
 constexpr int SG_MAXCL = 16;
 
@@ -105,7 +105,7 @@ __device__ __forceinline__ void sg_cluster_wait() {
 }
 
 // RT: the pooling radius when known at compile time (pooling in registers), or -1.
-// KPT: positions per thread (4, 8 or 16).
+// KPT: positions per thread (8, 16 or 32).
 template <int RT, int KPT>
 __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* __restrict__ scores, int Lk,
                                                                   int chunk, int radius_rt, int protect,
@@ -409,11 +409,11 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
 // Cluster size and chunk for a row of Lk positions; 0 if the row does not fit.
 // The largest cluster considered gives each CTA <= 4096 positions (up to 16 CTAs);
 // a cluster of half that size is the other candidate (see launch_cluster_select).
-static int sg_kpt(int chunk) { return chunk <= 4 * SG_NT ? 4 : (chunk <= 8 * SG_NT ? 8 : 16); }
+static int sg_kpt(int chunk) { return chunk <= 8 * SG_NT ? 8 : (chunk <= 16 * SG_NT ? 16 : 32); }
 
 static int sg_chunk(int Lk, int radius, int cl, int* chunk_out, size_t* smem_out) {
   const int chunk = (Lk + cl - 1) / cl;
-  if (chunk > 16 * SG_NT) return 0;
+  if (chunk > 32 * SG_NT) return 0;
   const size_t smem = ((size_t)sg_red_offset(chunk, radius, sg_kpt(chunk)) + 3 * (2048 / cl)) * 4;
   if (smem + sizeof(SgShared) > 227 * 1024) return 0;
   *chunk_out = chunk;
@@ -439,9 +439,9 @@ constexpr int SG_VARIANTS = 6;
 // kernel for the radius (5: the default kernel_size 11) and positions per thread
 static SgKernel sg_kernel(bool r5, int kpt, int* variant) {
   static const SgKernel table[SG_VARIANTS] = {
-      cluster_select_kernel<-1, 4>, cluster_select_kernel<-1, 8>, cluster_select_kernel<-1, 16>,
-      cluster_select_kernel<5, 4>,  cluster_select_kernel<5, 8>,  cluster_select_kernel<5, 16>};
-  *variant = (r5 ? 3 : 0) + (kpt == 4 ? 0 : (kpt == 8 ? 1 : 2));
+      cluster_select_kernel<-1, 8>, cluster_select_kernel<-1, 16>, cluster_select_kernel<-1, 32>,
+      cluster_select_kernel<5, 8>,  cluster_select_kernel<5, 16>,  cluster_select_kernel<5, 32>};
+  *variant = (r5 ? 3 : 0) + (kpt == 8 ? 0 : (kpt == 16 ? 1 : 2));
   return table[*variant];
 }
 
@@ -515,14 +515,14 @@ static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel
   if (cl > 1 && sg_chunk(Lk, radius, cl / 2, &chunk2, &smem2)) {
     // Rows run one cluster each; rows beyond the resident clusters wait for a
     // second wave. Estimated time per wave: a fixed ~6 us of barriers plus
-    // ~1.6 us per 1024 positions of a CTA's chunk (measured on B200).
+    // ~0.9 us per position of a thread (measured on B200).
     int variant2;
     SgKernel kern2 = sg_kernel(r5, sg_kpt(chunk2), &variant2);
     if ((rc = sg_prepare(kern2, variant2, smem2))) return rc;
     auto cost = [&](SgKernel kr, int var, int c, int ch, size_t sm) {
       const int act = sg_active_clusters(kr, var, c, sm);
       const int waves = (BH + act - 1) / act;
-      return waves * (6.0 + 1.6 * ch / 1024.0);
+      return waves * (6.0 + 0.9 * ch / (double)SG_NT);
     };
     if (cost(kern2, variant2, cl / 2, chunk2, smem2) < cost(kern, variant, cl, chunk, smem)) {
       cl /= 2;
