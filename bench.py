@@ -75,6 +75,9 @@ def parse_args():
     ap.add_argument("--ragged-seqs", type=int, default=16)
     ap.add_argument("--ragged-layers", type=int, default=32)
     ap.add_argument("--ragged-seed", type=int, default=5)
+    ap.add_argument("--ragged-batch", choices=["sequence", "unit"], default="sequence",
+                    help="ragged: one compress call per sequence over the rank's layers of it "
+                         "(B = layers), or one call per (sequence, layer) unit")
     return ap.parse_args()
 
 
@@ -408,12 +411,36 @@ def run_ragged(args, rank, n, world):
     parts = lpt_partition(all_units, n)
     mine = parts[rank]
     comps, work = {}, []
-    for u in mine:
-        wl = llama_layer(u.lk, keep_ratio=args.keep_ratio, seed=1000 * u.seq + u.layer + 7)
-        if u.lk not in comps:
-            comps[u.lk] = ops.Compressor(wl.B, wl.Hq, wl.Hkv, wl.Lq, wl.Lk, wl.D, wl.dtype, wl.window_size,
-                                         wl.kernel_size, wl.keep_len(), device=dev)
-        work.append((comps[u.lk], make_qkv(wl, dev)))
+    if args.ragged_batch == "unit":
+        for u in mine:
+            wl = llama_layer(u.lk, keep_ratio=args.keep_ratio, seed=1000 * u.seq + u.layer + 7)
+            if u.lk not in comps:
+                comps[u.lk] = ops.Compressor(wl.B, wl.Hq, wl.Hkv, wl.Lq, wl.Lk, wl.D, wl.dtype,
+                                             wl.window_size, wl.kernel_size, wl.keep_len(), device=dev)
+            work.append((comps[u.lk], make_qkv(wl, dev)))
+    else:
+        # the rank's layers of one sequence share Lk: one call over all their
+        # (layer, KV head) rows, the layers stacked along the batch axis
+        by_seq = {}
+        for u in mine:
+            by_seq.setdefault(u.seq, []).append(u)
+        for seq in sorted(by_seq, key=lambda q: -by_seq[q][0].lk):
+            units = sorted(by_seq[seq], key=lambda u: u.layer)
+            wl0 = llama_layer(units[0].lk, keep_ratio=args.keep_ratio)
+            L = len(units)
+            Q = torch.empty(L, wl0.Hq, wl0.Lq, wl0.D, dtype=wl0.dtype, device=dev)
+            K = torch.empty(L, wl0.Hkv, wl0.Lk, wl0.D, dtype=wl0.dtype, device=dev)
+            V = torch.empty_like(K)
+            for i, u in enumerate(units):  # the same per-unit data as the unit mode
+                q, k, v = make_qkv(llama_layer(u.lk, keep_ratio=args.keep_ratio,
+                                               seed=1000 * u.seq + u.layer + 7), dev)
+                Q[i].copy_(q[0])
+                K[i].copy_(k[0])
+                V[i].copy_(v[0])
+                del q, k, v
+            comp = ops.Compressor(L, wl0.Hq, wl0.Hkv, wl0.Lq, wl0.Lk, wl0.D, wl0.dtype, wl0.window_size,
+                                  wl0.kernel_size, wl0.keep_len(), device=dev)
+            work.append((comp, (Q, K, V)))
     stream = torch.cuda.current_stream(dev)
 
     def one_pass():
@@ -463,6 +490,7 @@ def run_ragged(args, rank, n, world):
                    "sequences_lk": lengths, "layers": args.ragged_layers, "Hq": 32, "Hkv": hkv, "D": 128,
                    "Lq": 8, "window": 8, "kernel_size": 11, "keep_ratio": args.keep_ratio,
                    "units": len(all_units), "units_per_rank": [len(p) for p in parts],
+                   "calls_per_pass_rank0": len(work), "batching": args.ragged_batch,
                    "load_imbalance": load_imbalance(parts),
                    "parallelism": f"{n} ranks, (sequence, layer) units, longest-first balance, no collective",
                    "l2": "distinct inputs per unit, whole batch far above the 126 MB L2"},

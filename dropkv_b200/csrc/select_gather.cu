@@ -445,40 +445,41 @@ static SgKernel sg_kernel(bool r5, int kpt, int* variant) {
   return table[*variant];
 }
 
-// Function attributes (dynamic shared memory, 16-CTA clusters), set once per device
-// and variant for the largest size used so far.
+// Function attributes, set once per device and variant: the largest dynamic
+// shared memory any chunk can ask for, and 16-CTA clusters.
 static int sg_prepare(SgKernel kern, int variant, size_t smem) {
   static unsigned long long done[SG_VARIANTS] = {};
-  static size_t done_smem[SG_VARIANTS][64] = {};
+  const int max_dyn = 227 * 1024 - (int)sizeof(SgShared);
+  if (smem > (size_t)max_dyn) return fail(DROPKV_ERR_UNSUPPORTED, "cluster select needs %zu bytes", smem);
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && (done[variant] & (1ull << dev)) && done_smem[variant][dev] >= smem) return DROPKV_OK;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %zu for the cluster select", smem);
+  if (dev < 64 && (done[variant] & (1ull << dev))) return DROPKV_OK;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn) != cudaSuccess)
+    return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %d for the cluster select", max_dyn);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
     return fail(DROPKV_ERR_CUDA, "cannot allow 16-CTA clusters for the cluster select");
-  if (dev < 64) {
-    done[variant] |= (1ull << dev);
-    done_smem[variant][dev] = smem;
-  }
+  if (dev < 64) done[variant] |= (1ull << dev);
   return DROPKV_OK;
 }
 
-// Clusters of `cl` CTAs that can be resident at once on this device (one CTA per
-// SM; a cluster must fit in one GPC, and GPCs differ in size), cached per device,
-// variant and cluster size for the shared-memory size last asked.
+// Clusters of `cl` CTAs that can be resident at once on this device (a cluster
+// must fit in one GPC, and GPCs differ in size), cached per device, variant,
+// cluster size and 8 KB step of dynamic shared memory (the query uses the step's
+// upper end, so the answer is never too high).
 static int sg_active_clusters(SgKernel kern, int variant, int cl, size_t smem) {
-  static int cache[SG_VARIANTS][5][64];
-  static size_t cache_smem[SG_VARIANTS][5][64];
+  constexpr int kDevs = 16, kSteps = 29;  // 29 steps of 8 KB cover 227 KB
+  static int cache[SG_VARIANTS][5][kDevs][kSteps];
   int dev = 0;
   cudaGetDevice(&dev);
   int lg = 0;
   while ((1 << lg) < cl) ++lg;
-  if (dev < 64 && cache[variant][lg][dev] > 0 && cache_smem[variant][lg][dev] == smem) return cache[variant][lg][dev];
+  const int step = (int)std::min<size_t>(kSteps - 1, smem / 8192);
+  const size_t smem_q = std::min<size_t>((size_t)(step + 1) * 8192, 227 * 1024 - sizeof(SgShared));  // <= max_dyn
+  if (dev < kDevs && cache[variant][lg][dev][step] > 0) return cache[variant][lg][dev][step];
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cl);
   cfg.blockDim = dim3(SG_NT);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = std::max(smem, smem_q);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cl;
@@ -491,10 +492,7 @@ static int sg_active_clusters(SgKernel kern, int variant, int cl, size_t smem) {
     cudaGetLastError();  // clear the query's error; assume every cluster is resident
     return 1 << 20;
   }
-  if (dev < 64) {
-    cache_smem[variant][lg][dev] = smem;
-    cache[variant][lg][dev] = n;
-  }
+  if (dev < kDevs) cache[variant][lg][dev][step] = n;
   return n;
 }
 
@@ -510,26 +508,34 @@ static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel
   SgKernel kern = sg_kernel(r5, sg_kpt(chunk), &variant);
   int rc = sg_prepare(kern, variant, smem);
   if (rc) return rc;
-  int chunk2 = 0;
-  size_t smem2 = 0;
-  if (cl > 1 && sg_chunk(Lk, radius, cl / 2, &chunk2, &smem2)) {
-    // Rows run one cluster each; rows beyond the resident clusters wait for a
-    // second wave. Estimated time per wave: a fixed ~6 us of barriers plus
-    // ~0.9 us per position of a thread (measured on B200).
-    int variant2;
-    SgKernel kern2 = sg_kernel(r5, sg_kpt(chunk2), &variant2);
-    if ((rc = sg_prepare(kern2, variant2, smem2))) return rc;
-    auto cost = [&](SgKernel kr, int var, int c, int ch, size_t sm) {
-      const int act = sg_active_clusters(kr, var, c, sm);
-      const int waves = (BH + act - 1) / act;
-      return waves * (6.0 + 0.9 * ch / (double)SG_NT);
-    };
-    if (cost(kern2, variant2, cl / 2, chunk2, smem2) < cost(kern, variant, cl, chunk, smem)) {
-      cl /= 2;
-      chunk = chunk2;
-      smem = smem2;
-      kern = kern2;
+  // Rows run one cluster each; rows beyond the resident clusters wait for another
+  // wave. Estimated time per wave: a fixed ~6 us of barriers plus ~0.9 us per
+  // position of a thread (measured on B200). Smaller clusters (more positions per
+  // thread) are considered only while the rows need more than one wave.
+  auto cost = [&](SgKernel kr, int var, int c, int ch, size_t sm, int* waves_out) {
+    const int act = sg_active_clusters(kr, var, c, sm);
+    *waves_out = (BH + act - 1) / act;
+    return *waves_out * (6.0 + 0.9 * ch / (double)SG_NT);
+  };
+  int waves;
+  double best = cost(kern, variant, cl, chunk, smem, &waves);
+  for (int c = cl / 2; c >= 1 && waves > 1; c /= 2) {
+    int ch;
+    size_t sm;
+    if (!sg_chunk(Lk, radius, c, &ch, &sm)) break;  // chunks only grow from here
+    int var;
+    SgKernel kr = sg_kernel(r5, sg_kpt(ch), &var);
+    if ((rc = sg_prepare(kr, var, sm))) return rc;
+    int w;
+    const double t = cost(kr, var, c, ch, sm, &w);
+    if (t < best) {
+      best = t;
+      cl = c;
+      chunk = ch;
+      smem = sm;
+      kern = kr;
     }
+    waves = w;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(BH * cl);
