@@ -239,6 +239,58 @@ __device__ __forceinline__ float round_p_t(float p) {
   return p;
 }
 
+// Paired fp32 arithmetic: one instruction for both lanes of a float2 (sm_100),
+// each lane rounded as the scalar instruction would round it.
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rc, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+      "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "add.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "sub.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "mul.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// 1/x by the hardware approximation (x here is in [eps, 1 + eps]).
+__device__ __forceinline__ float rcpf(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Two p rounded to the input dtype, as round_p_t does for one.
+template <int ROUND>
+__device__ __forceinline__ float2 round_p2(float2 p) {
+  if (ROUND == DROPKV_ROUND_BF16) {
+    uint32_t u;  // RNE of both in one conversion: x in the upper half, y in the lower
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(u) : "f"(p.x), "f"(p.y));
+    return make_float2(__uint_as_float(u & 0xffff0000u), __uint_as_float(u << 16));
+  }
+  if (ROUND == DROPKV_ROUND_F16) return __half22float2(__floats2half2_rn(p.x, p.y));
+  return p;
+}
+
 // C columns per lane (C a power of two <= 32): lane l returns column (l % C)
 // reduced over all 32 lanes.  log2(C) transpose steps, then the remaining lanes.
 template <int C, bool MAX>
@@ -288,8 +340,8 @@ __device__ __forceinline__ void store_p(uint8_t* hi_tile, uint8_t* lo_tile, int 
 #pragma unroll
   for (int j = 0; j < HC; j += 2) {
     hw[j / 2] = pack2<T>(ps[j], ps[j + 1]);
-    const float2 back = unpack2<T>(hw[j / 2]);
-    lw[j / 2] = pack2<T>(ps[j] - back.x, ps[j + 1] - back.y);
+    const float2 lo = f2_sub(make_float2(ps[j], ps[j + 1]), unpack2<T>(hw[j / 2]));
+    lw[j / 2] = pack2<T>(lo.x, lo.y);
   }
   if constexpr (HC == 4) {
     const uint32_t off = tc::swz_offset<PRB>(jkey, cbase);
@@ -634,11 +686,19 @@ __global__ void __launch_bounds__(NTH, 1)
         const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
         float ps[HC];
 #pragma unroll
-        for (int j = 0; j < HC; ++j) {
-          const bool ok = (edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j]) && ml[j] != -INFINITY;
-          const float pr = ok ? ex2f(fmaf(s[j], a.c, -ml[j])) : 0.f;
-          ssum[j] += pr;
-          ps[j] = pr * a.pscale;
+        for (int j = 0; j < HC; j += 2) {
+          const bool ok0 = (edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j]) && ml[j] != -INFINITY;
+          const bool ok1 =
+              (edge ? (key <= bnd_s[cbase + j + 1] && key < Lk) : colok[j + 1]) && ml[j + 1] != -INFINITY;
+          const float2 x = f2_fma(make_float2(s[j], s[j + 1]), make_float2(a.c, a.c),
+                                  make_float2(-ml[j], -ml[j + 1]));
+          const float2 pr = make_float2(ok0 ? ex2f(x.x) : 0.f, ok1 ? ex2f(x.y) : 0.f);
+          const float2 sm2 = f2_add(make_float2(ssum[j], ssum[j + 1]), pr);
+          ssum[j] = sm2.x;
+          ssum[j + 1] = sm2.y;
+          const float2 sc = f2_mul(pr, make_float2(a.pscale, a.pscale));
+          ps[j] = sc.x;
+          ps[j + 1] = sc.y;
         }
         uint8_t* pb = sm + L::PS + buf * 2 * L::PT;
         store_p<T, HC, PRB>(pb, pb + L::PT, jkey, cbase, ps);
@@ -653,7 +713,7 @@ __global__ void __launch_bounds__(NTH, 1)
           const uint32_t kpos = (uint32_t)rd * 3u * nt + (uint32_t)nt + (uint32_t)i;  // ring position
           const uint32_t slot = kpos % NS;
           wait_bar(&full[slot], (kpos / NS) & 1, 32);
-          float vn = 0.f;
+          float2 vn2 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int rr = 0; rr < NREG; ++rr) {
             const uint8_t* vt = sm + L::RING + slot * L::TILE + rr * 16384 + jkey * 128;
@@ -664,12 +724,11 @@ __global__ void __launch_bounds__(NTH, 1)
 #pragma unroll
               for (int k2 = 0; k2 < 4; ++k2) {
                 const float2 x = unpack2<T>(w4[k2]);
-                vn = fmaf(x.x, x.x, vn);
-                vn = fmaf(x.y, x.y, vn);
+                vn2 = f2_fma(x, x, vn2);
               }
             }
           }
-          vn_s[i * TK + jkey] = vn;
+          vn_s[i * TK + jkey] = vn2.x + vn2.y;
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(&freeb[slot]);
         }
@@ -908,23 +967,28 @@ __global__ void __launch_bounds__(NTH, 1)
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bx[B_S2FREE0]);
-#pragma unroll
-        for (int j = 0; j < HC; ++j) s2[j] += s2l[j];
         const int key = (t0 + i) * TK + jkey;
         const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
-        float sw = 0.f, sb = 0.f, sc = 0.f;
+        // pairs of query columns: w = (p / (1 - p + eps))^2 with p rounded to the
+        // input dtype; sums of w, w <v, y> and w ||y||^2 over this thread's columns
+        float2 sw2 = make_float2(0.f, 0.f), sb2 = sw2, sc2 = sw2;
 #pragma unroll
-        for (int j = 0; j < HC; ++j) {
-          const bool ok = edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j];
-          float pr = ex2f(fmaf(s[j], a.c, -lsel[j]));
-          pr = fminf(pr, 1.f);
-          pr = round_p_t<ROUND>(pr);
-          const float ratio = __fdividef(pr, 1.f - pr + p.eps);
-          const float w = ok ? ratio * ratio : 0.f;
-          sw += w;
-          sb = fmaf(w, s2[j], sb);
-          sc = fmaf(w, ynl[j], sc);
+        for (int j = 0; j < HC; j += 2) {
+          const bool ok0 = edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j];
+          const bool ok1 = edge ? (key <= bnd_s[cbase + j + 1] && key < Lk) : colok[j + 1];
+          const float2 x = f2_fma(make_float2(s[j], s[j + 1]), make_float2(a.c, a.c),
+                                  make_float2(-lsel[j], -lsel[j + 1]));
+          const float2 pr = round_p2<ROUND>(make_float2(fminf(ex2f(x.x), 1.f), fminf(ex2f(x.y), 1.f)));
+          const float2 den = f2_add(f2_sub(make_float2(1.f, 1.f), pr), make_float2(p.eps, p.eps));
+          const float2 ratio = f2_mul(pr, make_float2(rcpf(den.x), rcpf(den.y)));
+          float2 w = f2_mul(ratio, ratio);
+          w.x = ok0 ? w.x : 0.f;
+          w.y = ok1 ? w.y : 0.f;
+          sw2 = f2_add(sw2, w);
+          sb2 = f2_fma(w, f2_add(make_float2(s2[j], s2[j + 1]), make_float2(s2l[j], s2l[j + 1])), sb2);
+          sc2 = f2_fma(w, make_float2(ynl[j], ynl[j + 1]), sc2);
         }
+        float sw = sw2.x + sw2.y, sb = sb2.x + sb2.y, sc = sc2.x + sc2.y;
         // column groups 1-3 hand their sums to group 0 (fixed order: deterministic)
         float* xb = xch + buf * 9 * TK;
         if (cg > 0) {
