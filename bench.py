@@ -64,10 +64,11 @@ def parse_args():
     ap.add_argument("--keep-ratio", type=float, default=0.1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["layer", "ragged", "chunked"], default="layer",
+    ap.add_argument("--workload", choices=["layer", "ragged", "chunked", "decode"], default="layer",
                     help="layer: one Llama layer per rank (default, weak scaling); ragged: the "
                          "config-5 batch split across ranks (strong scaling); chunked: config-4 "
-                         "chunked prefill through DropKVCache / prefill_chunked (1 GPU)")
+                         "chunked prefill through DropKVCache / prefill_chunked (1 GPU); decode: "
+                         "token steps over 32 compressed Llama layer caches (1 GPU)")
     ap.add_argument("--chunked-layers", type=int, default=32)
     ap.add_argument("--chunk", type=int, default=4096)
     ap.add_argument("--storage", choices=["cat", "buffer"], default="cat",
@@ -638,6 +639,138 @@ def run_chunked(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# decode over the compressed cache (scope row f2)
+# ---------------------------------------------------------------------------
+DECODE_METRIC = "decode token steps/sec over the compressed cache, 32 Llama-3.1-8B layers"
+
+
+def run_decode(args):
+    """One step = one new token through 32 layers: its K/V row appended in place to
+    each layer's compressed cache (row buffers) and attention of its 32 query heads
+    over the cache. ``value`` replays the 32-layer step as a CUDA graph (how a
+    decode loop runs without per-call host cost); the eager step through the same
+    calls and the reference's decode path (torch.cat of the cache and the token,
+    dropkv_cache.py:609-617, then torch's SDPA) are timed beside it."""
+    import torch
+    import torch.nn.functional as F
+    from dropkv_b200 import _lib, ops
+    from dropkv_b200.workloads import llama_layer
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = args.chunked_layers
+    wl = llama_layer(args.lk, keep_ratio=args.keep_ratio)
+    L0 = wl.keep_len()  # compressed length after the prefill eviction
+    B, Hq, Hkv, D = 1, 32, 8, 128
+    cap = L0 + args.warmup + 2 * args.steps + 8
+    g = torch.Generator(device=dev).manual_seed(3)
+    bufs = []
+    for _ in range(layers):
+        k = torch.randn(B, Hkv, cap, D, device=dev, generator=g).bfloat16()
+        v = torch.randn(B, Hkv, cap, D, device=dev, generator=g).bfloat16()
+        bufs.append((k, v))
+    n_tok = args.warmup + 2 * args.steps
+    toks = [(torch.randn(B, Hq, 1, D, device=dev, generator=g).bfloat16(),
+             torch.randn(B, Hkv, 1, D, device=dev, generator=g).bfloat16(),
+             torch.randn(B, Hkv, 1, D, device=dev, generator=g).bfloat16()) for _ in range(n_tok)]
+    ws = ops.decode_attention_workspace(B, Hq, Hkv, 1, cap, D, dev)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+
+    def append(layer, n, kn, vn):
+        k, v = bufs[layer]
+        rc = lib.dropkv_append_rows(k.data_ptr(), v.data_ptr(), cap * D, n, kn.data_ptr(), vn.data_ptr(), D, 1,
+                                    D, 2, B * Hkv, torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(rc, "dropkv_append_rows")
+
+    def step(t, n, attn):
+        q, kn, vn = toks[t]
+        out = None
+        for layer in range(layers):
+            k, v = bufs[layer]
+            if attn == "ours":
+                append(layer, n, kn, vn)
+                out = ops.decode_attention(q, k[:, :, :n + 1], v[:, :, :n + 1], workspace=ws)
+            else:  # the reference: a new tensor per token, then the model's SDPA
+                kc = torch.cat([k[:, :, :n], kn], dim=2)
+                vc = torch.cat([v[:, :, :n], vn], dim=2)
+                out = F.scaled_dot_product_attention(q, kc, vc, enable_gqa=True)
+        return out
+
+    def timed(attn, t0, n0):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = _lib.launch_count()
+        e0.record(stream)
+        for i in range(args.steps):
+            step(t0 + i, n0 + i, attn)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / args.steps, (_lib.launch_count() - l0) // args.steps
+
+    for i in range(args.warmup):
+        step(i, L0 + i, "ours")
+        step(i, L0 + i, "sdpa")
+    # both arms start from the same cache length
+    n0 = L0 + args.warmup
+    eager_ms, launches = timed("ours", args.warmup, n0)
+    sdpa_ms, _ = timed("sdpa", args.warmup + args.steps, n0)
+    # the same 32-layer step captured once and replayed (fixed cache length)
+    ng = n0 + args.steps
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        step(0, ng, "ours")  # warm the path on the capture stream
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(0, ng, "ours")
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(gpu_uuid(dev))
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    ours_ms = e0.elapsed_time(e1) / args.steps
+    del graph
+    # parity of the last step against torch (fp32 reference)
+    q = toks[0][0]
+    k, v = bufs[0]
+    n = n0 + args.steps
+    got = ops.decode_attention(q, k[:, :, :n], v[:, :, :n], workspace=ws).float()
+    ref = F.scaled_dot_product_attention(q.float(), k[:, :, :n].float(), v[:, :, :n].float(), enable_gqa=True)
+    max_err = float((got - ref).abs().max())
+    kv_bytes = layers * B * Hkv * (ng + 1) * D * 2 * 2
+    peak, peak_kind = measured_peaks()
+    gbs = kv_bytes / (ours_ms / 1e3) / 1e9
+    line = {
+        "metric": DECODE_METRIC, "value": 1e3 / ours_ms, "unit": "token steps/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ours_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) caches)",
+        "config": {"workload": f"decode_{layers}layers_cache{L0}", "layers": layers, "B": B, "Hq": Hq,
+                   "Hkv": Hkv, "D": D, "cache_len": ng + 1, "compressed_from": args.lk,
+                   "keep_ratio": args.keep_ratio, "storage": "row buffers, in-place append",
+                   "timing": "32-layer step (2 appends + 1 attention launch per layer) as a CUDA graph"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "traffic": None, "kernel": "whole step (appends + decode attention), K/V read once",
+                     "algorithmic_bytes": kv_bytes, "ms": ours_ms,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+        "eager": {"ms_per_step": eager_ms, "what": "the same calls from Python, one step after another "
+                                                   "(cache length growing by one per step)"},
+        "reference_path": {"ms_per_step": sdpa_ms, "what": "torch.cat of cache and token per layer "
+                                                           "(dropkv_cache.py:609-617), torch SDPA (enable_gqa)"},
+        "max_abs_err_vs_fp32": max_err, "cpu_baseline": None, "e2e": None, "gpu_launches": launches,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1")) > 1
@@ -646,11 +779,11 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, n)
         return
-    if args.workload == "chunked":
+    if args.workload in ("chunked", "decode"):
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         if rank == 0:
-            run_chunked(args)
+            (run_chunked if args.workload == "chunked" else run_decode)(args)
         return
     import torch
     import torch.distributed as dist

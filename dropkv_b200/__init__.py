@@ -13,13 +13,14 @@ Public API (the reference's names and semantics):
 
 from ._lib import DropKVError, version
 from .cache import Cache, DropKVCache, DynamicCache, prefill_chunked
-from .ops import compress, dropkv_scores_cuda, gather_compressed, scores, select_keep_indices
+from .ops import (compress, decode_attention, dropkv_scores_cuda, gather_compressed, scores,
+                  select_keep_indices)
 
 # Name of the reference entry point (dropkv_triton.py:643) for drop-in imports.
 dropkv_scores_triton = dropkv_scores_cuda
 
 __all__ = [
     "Cache", "DynamicCache", "DropKVCache", "prefill_chunked", "DropKVError", "version",
-    "compress", "dropkv_scores_cuda", "dropkv_scores_triton", "gather_compressed", "scores",
-    "select_keep_indices",
+    "compress", "decode_attention", "dropkv_scores_cuda", "dropkv_scores_triton", "gather_compressed",
+    "scores", "select_keep_indices",
 ]

@@ -47,6 +47,10 @@ SIGNATURES = {
                                          _c_p, _c_sz, _c_p]),
     "dropkv_append_rows": (_c_int, [_c_p, _c_p, _c_i64, _c_int, _c_p, _c_p, _c_i64, _c_int, _c_int, _c_int,
                                     _c_int, _c_p]),
+    "dropkv_decode_attention_workspace_size": (_c_sz, [_c_int] * 6),
+    "dropkv_decode_attention": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_i64,
+                                         _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_p,
+                                         _c_p, _c_sz, _c_p]),
     "dropkv_compress": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_int,
                                  _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int,
                                  _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz,

@@ -383,4 +383,30 @@ int dropkv_append_rows(void* k_dst, void* v_dst, int64_t dst_head_stride, int ds
   return DROPKV_OK;
 }
 
+size_t dropkv_decode_attention_workspace_size(int B, int Hq, int Hkv, int Lq, int L, int D) {
+  if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv || Lq < 1 || L < Lq || (D != 64 && D != 128)) return 0;
+  return decode_attention_workspace_size(B, Hq, Hkv, Lq, L, D);
+}
+
+int dropkv_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                            const void* k, const void* v, int64_t kv_sb, int64_t kv_sh, int dtype, int B, int Hq,
+                            int Hkv, int L, int D, float scale, void* out, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (!q || !k || !v || !out) return fail(DROPKV_ERR_ARG, "NULL pointer argument");
+  if (dtype != DROPKV_DTYPE_BF16 && dtype != DROPKV_DTYPE_F16)
+    return fail(DROPKV_ERR_UNSUPPORTED, "decode attention takes bf16 or fp16 inputs");
+  if (D != 64 && D != 128) return fail(DROPKV_ERR_UNSUPPORTED, "decode attention needs D of 64 or 128 (got %d)", D);
+  if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv) return fail(DROPKV_ERR_ARG, "invalid head counts Hq=%d Hkv=%d", Hq, Hkv);
+  if (Lq < 1 || L < Lq) return fail(DROPKV_ERR_ARG, "need 1 <= Lq <= L (Lq=%d, L=%d)", Lq, L);
+  if ((int64_t)B * Hkv > 65535) return fail(DROPKV_ERR_ARG, "B*Hkv exceeds 65535");
+  if (kv_sh < (int64_t)L * D || kv_sb < (int64_t)Hkv * kv_sh) return fail(DROPKV_ERR_ARG, "K/V strides too small");
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % 16 || (kv_sh * 2) % 16 || (kv_sb * 2) % 16)
+    return fail(DROPKV_ERR_ARG, "K/V rows must start on 16-byte boundaries");
+  if (!(scale > 0.f)) return fail(DROPKV_ERR_ARG, "scale must be positive");
+  int rc = check_ws(workspace, workspace_bytes, dropkv_decode_attention_workspace_size(B, Hq, Hkv, Lq, L, D));
+  if (rc) return rc;
+  return launch_decode_attention(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, kv_sb, kv_sh, dtype, B, Hq, Hkv, L, D, scale,
+                                 out, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

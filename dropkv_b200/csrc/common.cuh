@@ -113,6 +113,12 @@ SelectPlan plan_select(int BH, int Lk);
 int launch_select(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
                   int64_t* keep_idx, void* ws, cudaStream_t st);
 bool select_gather_supported(int Lk, int kernel_size);
+
+// Decode attention over the (compressed) cache (decode_attn.cu).
+size_t decode_attention_workspace_size(int B, int Hq, int Hkv, int Lq, int L, int D);
+int launch_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                            const void* k, const void* v, int64_t kv_sb, int64_t kv_sh, int dtype, int B, int Hq,
+                            int Hkv, int L, int D, float scale, void* out, void* ws, cudaStream_t st);
 // k == nullptr: selection only (keep_idx), no gather
 // in_sh / out_sh: elements between consecutive heads of K/V and of K_c/V_c
 // (0: contiguous, Lk * D and keep_len * D)

@@ -73,6 +73,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, uint64_t
 // ---------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ---------------------------------------------------------------------------
+// Untiled bulk copy of `bytes` contiguous bytes global -> this CTA's shared memory,
+// completing on `bar` (both addresses 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

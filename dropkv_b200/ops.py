@@ -266,6 +266,59 @@ def compress_strided(Q: torch.Tensor, K_buf: torch.Tensor, V_buf: torch.Tensor, 
     return idx
 
 
+_DA_WS: dict = {}  # per device: zero-initialised decode-attention workspace (kept zeroed by the library)
+
+
+def decode_attention_workspace(B: int, Hq: int, Hkv: int, Lq: int, L: int, D: int, device) -> torch.Tensor:
+    """A zero-filled workspace for ``decode_attention`` of this shape (fresh)."""
+    n = _lib.load().dropkv_decode_attention_workspace_size(B, Hq, Hkv, Lq, L, D)
+    return torch.zeros(max(int(n), 1), dtype=torch.uint8, device=device)
+
+
+def decode_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: float | None = None,
+                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention of the Lq query rows over the cached keys: [B, Hq, Lq, D] ->
+    [B, Hq, Lq, D], softmax(scale Q K^T) V per KV-head group, the query rows
+    tail-aligned to the L keys (row i sees keys j <= L - Lq + i).
+
+    This is what the model computes over the K/V that ``DropKVCache.update``
+    returns during decode (dropkv_cache.py:609-617 append the token; the model's
+    SDPA attends). K and V may be views into row buffers with spare capacity
+    (rows of D contiguous elements, any head and batch stride), as
+    ``DropKVCache(storage="buffer")`` hands out. ``workspace`` must be zero-filled
+    before its first use (``decode_attention_workspace``); the library leaves it
+    zeroed, so it can be reused, but not by calls running concurrently on two
+    streams. Without one, a per-device workspace is kept here.
+    """
+    _require_cuda(Q, K, V)
+    if Q.dim() != 4 or K.dim() != 4 or K.shape != V.shape:
+        raise ValueError("expected Q [B,Hq,Lq,D] and K, V [B,Hkv,L,D] of one shape")
+    if not (Q.dtype == K.dtype == V.dtype) or Q.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError("decode attention takes bf16 or fp16 Q, K and V of one dtype")
+    B, Hq, Lq, D = Q.shape
+    _, Hkv, L, _ = K.shape
+    if K.shape[0] != B or K.shape[3] != D or Hq % Hkv:
+        raise ValueError(f"shape mismatch: Q {tuple(Q.shape)}, K {tuple(K.shape)}")
+    if K.stride() != V.stride() or K.stride(3) != 1 or K.stride(2) != D:
+        raise ValueError("K and V need rows of D contiguous elements and equal strides")
+    scale = float(D ** -0.5 if scale is None else scale)
+    lib = _lib.load()
+    dev = Q.device
+    need = lib.dropkv_decode_attention_workspace_size(B, Hq, Hkv, Lq, L, D)
+    if workspace is None:
+        workspace = _DA_WS.get(dev)
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.zeros(max(int(need), 1), dtype=torch.uint8, device=dev)
+            _DA_WS[dev] = workspace
+    out = torch.empty(B, Hq, Lq, D, dtype=Q.dtype, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.dropkv_decode_attention(Q.data_ptr(), *Q.stride(), Lq, K.data_ptr(), V.data_ptr(), K.stride(0),
+                                         K.stride(1), _DTYPE_CODE[Q.dtype], B, Hq, Hkv, L, D, scale,
+                                         out.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream(dev))
+        _lib.check(rc, "dropkv_decode_attention")
+    return out
+
+
 def inv_sqrt_d(D: int) -> float:
     return 1.0 / math.sqrt(D)
 

@@ -184,6 +184,22 @@ DROPKV_API int dropkv_append_rows(void* k_dst, void* v_dst, int64_t dst_head_str
                                   const void* k_src, const void* v_src, int64_t src_head_stride, int rows,
                                   int D, int elem_bytes, int BH, void* stream);
 
+/* Decode attention over the (compressed) cache: out[b, h, i, :] =
+ * softmax(scale * q[b, h, i, :] . K[b, h / (Hq / Hkv), j, :]) V[b, h / (Hq / Hkv), j, :]
+ * over the keys j <= L - Lq + i (the Lq query rows tail-aligned to the L keys).
+ * Replaces the attention the model runs over the K/V that DropKVCache.update
+ * returns (dropkv_cache.py:609-617 append the decode token to the compressed
+ * cache; the model's SDPA attends over it). k/v: rows of D contiguous elements,
+ * kv_sh elements between KV heads and kv_sb between sequences (a row buffer with
+ * spare capacity is read in place), 16-byte aligned rows. bf16 or fp16, D 64 or
+ * 128; out [B, Hq, Lq, D] contiguous in the input dtype. The workspace must be
+ * zero-filled before its first use; every call leaves it ready for the next. */
+DROPKV_API size_t dropkv_decode_attention_workspace_size(int B, int Hq, int Hkv, int Lq, int L, int D);
+DROPKV_API int dropkv_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd,
+                                       int Lq, const void* k, const void* v, int64_t kv_sb, int64_t kv_sh,
+                                       int dtype, int B, int Hq, int Hkv, int L, int D, float scale, void* out,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
 /* Diagnostic: one 128-row tile through a tcgen05 MMA form used by the fused
  * scorer (mode 0: out[128][n] = A[128][128] B[n][128]^T with A loaded by TMA;
  * mode 1: out[128][n] = A[128][128]^T B[n][128]^T with A read MN-major; modes 2/3:
