@@ -365,7 +365,9 @@ __global__ void __launch_bounds__(NTH, 1)
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int NREG = D / 64;            // 64-wide slabs of a K/V/Q/Y row
   constexpr int TMAX = L::TMAX;
-  constexpr int S2COL = TMAX * NPAD;      // y^T accumulator / S2: 2*NPAD columns (hi part, lo part)
+  // 2*NPAD columns after the logit tiles: the y^T accumulator of pass 1, then S2
+  // of pass 2 (hi part, lo part each)
+  constexpr int S2COL = TMAX * NPAD;
   constexpr int HC = NPAD / 4;            // query columns per epilogue warp
   constexpr int PRB = L::PRB;
   static_assert(TMAX <= kMaxTiles, "s_done barriers");
@@ -513,9 +515,14 @@ __global__ void __launch_bounds__(NTH, 1)
       constexpr uint32_t ID_QK = tc::idesc_f16(BF16, 128, NPAD, false, false);
       // hi and lo halves stacked along N: one MMA per k-step reads the V tile once
       constexpr uint32_t ID_PV = tc::idesc_f16(BF16, 128, 2 * NPAD, true, true);
+      // S2 = V [y_hi | y_lo]^T: the halves stacked along N (one MMA per k-step; the
+      // tensor core's time here grows with the number of MMAs, not with N)
       constexpr uint32_t ID_S2 = tc::idesc_f16(BF16, 128, 2 * NPAD, false, false);
       constexpr uint32_t LBO_PV = (NREG == 2) ? 16384u : 0u;
       constexpr uint32_t LAYOUT_P = tc::layout_for_row_bytes(PRB);
+      // descriptors of the Q and y operands; per k-step offsets are added to them
+      const uint64_t qd0 = tc::smem_desc(qs0, 16, 1024);
+      const uint64_t yd0 = tc::smem_desc(ys0, 16, 1024);
       uint32_t k = 0;  // ring position
       uint32_t c_pready[2] = {0, 0}, c_s2free[2] = {0, 0};
       for (int rd = 0; rd < my_rounds && !*vabort; ++rd) {
@@ -526,11 +533,11 @@ __global__ void __launch_bounds__(NTH, 1)
           const uint32_t slot = k % NS;
           if (!wait_bar(&full[slot], (k / NS) & 1, 21)) break;
           tc::tc_fence_after();
-          const uint32_t a0 = ring0 + slot * L::TILE;
+          const uint64_t ad0 = tc::smem_desc(ring0 + slot * L::TILE, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t ad = tc::smem_desc(a0 + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024);
-            const uint64_t bd = tc::smem_desc(qs0 + (kk / 4) * L::RB + (kk % 4) * 32, 16, 1024);
+            const uint64_t ad = tc::desc_add(ad0, (kk / 4) * 16384 + (kk % 4) * 32);
+            const uint64_t bd = tc::desc_add(qd0, (kk / 4) * L::RB + (kk % 4) * 32);
             tc::mma_f16(tmem + i * NPAD, ad, bd, ID_QK, kk > 0);
           }
           tc::mma_commit(&freeb[slot]);
@@ -545,13 +552,13 @@ __global__ void __launch_bounds__(NTH, 1)
           if (!wait_bar(&bx[B_PREADY0 + buf], c_pready[buf] & 1, 23)) break;
           ++c_pready[buf];
           tc::tc_fence_after();
-          const uint32_t a0 = ring0 + slot * L::TILE;
-          const uint32_t pb = ps0 + buf * 2 * L::PT;
+          const uint64_t ad0 = tc::smem_desc(ring0 + slot * L::TILE, LBO_PV, 1024);
+          const uint64_t bd0 = tc::smem_desc(ps0 + buf * 2 * L::PT, L::PT, 8 * PRB, LAYOUT_P);
           // B: the P_hi tile and, one leading-byte-offset (a tile) further, P_lo
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = tc::smem_desc(a0 + kk * 2048, LBO_PV, 1024);
-            const uint64_t bd = tc::smem_desc(pb + kk * 16 * PRB, L::PT, 8 * PRB, LAYOUT_P);
+            const uint64_t ad = tc::desc_add(ad0, kk * 2048);
+            const uint64_t bd = tc::desc_add(bd0, kk * 16 * PRB);
             tc::mma_f16(tmem + S2COL, ad, bd, ID_PV, (i > 0 || kk > 0) ? 1u : 0u);
           }
           tc::mma_commit(&freeb[slot]);  // + the ||v||^2 warps' arrivals
@@ -569,19 +576,20 @@ __global__ void __launch_bounds__(NTH, 1)
             ++c_s2free[0];
           }
           tc::tc_fence_after();
-          const uint32_t a0 = ring0 + slot * L::TILE;
-          // B: y_hi rows then y_lo rows of each 64-wide slab (N = 2 * NPAD)
+          const uint64_t ad0 = tc::smem_desc(ring0 + slot * L::TILE, 16, 1024);
+          // B: the y_hi rows then the y_lo rows of each 64-wide slab (N = 2 * NPAD)
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint64_t ad = tc::smem_desc(a0 + (kk / 4) * 16384 + (kk % 4) * 32, 16, 1024);
-            const uint64_t bd = tc::smem_desc(ys0 + (kk / 4) * 2 * L::RB + (kk % 4) * 32, 16, 1024);
+            const uint64_t ad = tc::desc_add(ad0, (kk / 4) * 16384 + (kk % 4) * 32);
+            const uint64_t bd = tc::desc_add(yd0, (kk / 4) * 2 * L::RB + (kk % 4) * 32);
             tc::mma_f16(tmem + S2COL, ad, bd, ID_S2, kk > 0 ? 1u : 0u);
           }
           tc::mma_commit(&freeb[slot]);
           tc::mbar_arrive_cnt(&freeb[slot], kVnWarps);
           tc::mma_commit(&bx[B_S2READY0]);
         }
-        // the last S2 is released after this round's epilogue
+        // the last S2 is released after this round's epilogue read it (and every
+        // logit tile of the round before it)
         if (nt > 0) {
           if (!wait_bar(&bx[B_S2FREE0], c_s2free[0] & 1, 27)) break;
           ++c_s2free[0];
@@ -604,9 +612,10 @@ __global__ void __launch_bounds__(NTH, 1)
       if (stamper) a.trace[3 + ((size_t)blockIdx.x * a.rounds + rd) * kTraceEv + ev] = tc::globaltimer_ns();
     };
     // which of my columns are real query rows
-    bool colok[HC];
-#pragma unroll
-    for (int j = 0; j < HC; ++j) colok[j] = (cbase + j) < M;
+    // (column j of this warp is a real query row when cbase + j < M)
+    // every column of this warp is a real query row: tiles below the causal edge
+    // then need no per-pair masks (the fast loops below)
+    const bool allcols = cbase + HC <= M;
 
     for (int rd = 0; rd < my_rounds; ++rd) {
       const int h = rd * a.groups + grp;
@@ -645,12 +654,21 @@ __global__ void __launch_bounds__(NTH, 1)
         tmem_ld<HC>(tmem + lrow + i * NPAD + cbase, s);
         const int key = (t0 + i) * TK + jkey;
         const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
+        // max of the raw logits; scaled by c > 0 after the loop (rounding is
+        // monotonic, so max(l) * c is the max of the rounded l * c)
+        if (!edge && allcols) {
 #pragma unroll
-        for (int j = 0; j < HC; ++j) {
-          const bool ok = edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j];
-          mx[j] = fmaxf(mx[j], ok ? s[j] * a.c : -INFINITY);
+          for (int j = 0; j < HC; ++j) mx[j] = fmaxf(mx[j], s[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < HC; ++j) {
+            const bool ok = edge ? (key <= bnd_s[cbase + j] && key < Lk) : (cbase + j < M);
+            mx[j] = fmaxf(mx[j], ok ? s[j] : -INFINITY);
+          }
         }
       }
+#pragma unroll
+      for (int j = 0; j < HC; ++j) mx[j] *= a.c;
       stamp(rd, TR_LOGITS);
       {
         const float col = col_reduce<HC, true>(mx, lane);
@@ -670,9 +688,9 @@ __global__ void __launch_bounds__(NTH, 1)
       float ssum[HC];
 #pragma unroll
       for (int j = 0; j < HC; ++j) ssum[j] = 0.f;
-      float ml[HC];
+      float nml[HC];  // minus the row maxima
 #pragma unroll
-      for (int j = 0; j < HC; ++j) ml[j] = mloc[cbase + j];
+      for (int j = 0; j < HC; ++j) nml[j] = -mloc[cbase + j];
       for (int i = 0; i < nt; ++i) {
         const int buf = i % NPB;
         if (i >= NPB) {
@@ -685,20 +703,36 @@ __global__ void __launch_bounds__(NTH, 1)
         const int key = (t0 + i) * TK + jkey;
         const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
         float ps[HC];
+        if (!edge && allcols) {
+          // every pair is a valid (key, query row) and the row maxima are finite
 #pragma unroll
-        for (int j = 0; j < HC; j += 2) {
-          const bool ok0 = (edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j]) && ml[j] != -INFINITY;
-          const bool ok1 =
-              (edge ? (key <= bnd_s[cbase + j + 1] && key < Lk) : colok[j + 1]) && ml[j + 1] != -INFINITY;
-          const float2 x = f2_fma(make_float2(s[j], s[j + 1]), make_float2(a.c, a.c),
-                                  make_float2(-ml[j], -ml[j + 1]));
-          const float2 pr = make_float2(ok0 ? ex2f(x.x) : 0.f, ok1 ? ex2f(x.y) : 0.f);
-          const float2 sm2 = f2_add(make_float2(ssum[j], ssum[j + 1]), pr);
-          ssum[j] = sm2.x;
-          ssum[j + 1] = sm2.y;
-          const float2 sc = f2_mul(pr, make_float2(a.pscale, a.pscale));
-          ps[j] = sc.x;
-          ps[j + 1] = sc.y;
+          for (int j = 0; j < HC; j += 2) {
+            const float2 x = f2_fma(make_float2(s[j], s[j + 1]), make_float2(a.c, a.c),
+                                    make_float2(nml[j], nml[j + 1]));
+            const float2 pr = make_float2(ex2f(x.x), ex2f(x.y));
+            const float2 sm2 = f2_add(make_float2(ssum[j], ssum[j + 1]), pr);
+            ssum[j] = sm2.x;
+            ssum[j + 1] = sm2.y;
+            const float2 sc = BF16 ? pr : f2_mul(pr, make_float2(a.pscale, a.pscale));
+            ps[j] = sc.x;
+            ps[j + 1] = sc.y;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < HC; j += 2) {
+            const bool ok0 = (edge ? (key <= bnd_s[cbase + j] && key < Lk) : (cbase + j < M)) && nml[j] != INFINITY;
+            const bool ok1 =
+                (edge ? (key <= bnd_s[cbase + j + 1] && key < Lk) : (cbase + j + 1 < M)) && nml[j + 1] != INFINITY;
+            const float2 x = f2_fma(make_float2(s[j], s[j + 1]), make_float2(a.c, a.c),
+                                    make_float2(nml[j], nml[j + 1]));
+            const float2 pr = make_float2(ok0 ? ex2f(x.x) : 0.f, ok1 ? ex2f(x.y) : 0.f);
+            const float2 sm2 = f2_add(make_float2(ssum[j], ssum[j + 1]), pr);
+            ssum[j] = sm2.x;
+            ssum[j + 1] = sm2.y;
+            const float2 sc = f2_mul(pr, make_float2(a.pscale, a.pscale));
+            ps[j] = sc.x;
+            ps[j + 1] = sc.y;
+          }
         }
         uint8_t* pb = sm + L::PS + buf * 2 * L::PT;
         store_p<T, HC, PRB>(pb, pb + L::PT, jkey, cbase, ps);
@@ -767,7 +801,7 @@ __global__ void __launch_bounds__(NTH, 1)
           }
 #pragma unroll
           for (int j = 0; j < HC; ++j)
-            if (colok[j]) __stcg(a.part_y + (prow + cbase + j) * D + d, nt > 0 ? (v[j] + vl[j]) * inv : 0.f);
+            if (cbase + j < M) __stcg(a.part_y + (prow + cbase + j) * D + d, nt > 0 ? (v[j] + vl[j]) * inv : 0.f);
         }
       }
       tc::tc_fence_before();
@@ -949,10 +983,10 @@ __global__ void __launch_bounds__(NTH, 1)
       stamp(rd, TR_YSTAGE);
 
       // ---- pass 2: score epilogue over S (TMEM, pass 1), S2 = <v, y> and ||v||^2 (pass 1c) ----
-      float lsel[HC], ynl[HC];
+      float nlse[HC], ynl[HC];
 #pragma unroll
       for (int j = 0; j < HC; ++j) {
-        lsel[j] = lse_s[cbase + j];
+        nlse[j] = -lse_s[cbase + j];
         ynl[j] = yn_s[cbase + j];
       }
       for (int i = 0; i < nt; ++i) {
@@ -967,26 +1001,52 @@ __global__ void __launch_bounds__(NTH, 1)
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bx[B_S2FREE0]);
+#pragma unroll
+        for (int j = 0; j < HC; j += 2) {  // <v, y> = <v, y_hi> + <v, y_lo>
+          const float2 t = f2_add(make_float2(s2[j], s2[j + 1]), make_float2(s2l[j], s2l[j + 1]));
+          s2[j] = t.x;
+          s2[j + 1] = t.y;
+        }
         const int key = (t0 + i) * TK + jkey;
         const bool edge = (t0 + i) * TK + TK - 1 > Lk - W;
         // pairs of query columns: w = (p / (1 - p + eps))^2 with p rounded to the
         // input dtype; sums of w, w <v, y> and w ||y||^2 over this thread's columns
         float2 sw2 = make_float2(0.f, 0.f), sb2 = sw2, sc2 = sw2;
+        if (!edge && allcols) {
 #pragma unroll
-        for (int j = 0; j < HC; j += 2) {
-          const bool ok0 = edge ? (key <= bnd_s[cbase + j] && key < Lk) : colok[j];
-          const bool ok1 = edge ? (key <= bnd_s[cbase + j + 1] && key < Lk) : colok[j + 1];
-          const float2 x = f2_fma(make_float2(s[j], s[j + 1]), make_float2(a.c, a.c),
-                                  make_float2(-lsel[j], -lsel[j + 1]));
-          const float2 pr = round_p2<ROUND>(make_float2(fminf(ex2f(x.x), 1.f), fminf(ex2f(x.y), 1.f)));
-          const float2 den = f2_add(f2_sub(make_float2(1.f, 1.f), pr), make_float2(p.eps, p.eps));
-          const float2 ratio = f2_mul(pr, make_float2(rcpf(den.x), rcpf(den.y)));
-          float2 w = f2_mul(ratio, ratio);
-          w.x = ok0 ? w.x : 0.f;
-          w.y = ok1 ? w.y : 0.f;
-          sw2 = f2_add(sw2, w);
-          sb2 = f2_fma(w, f2_add(make_float2(s2[j], s2[j + 1]), make_float2(s2l[j], s2l[j + 1])), sb2);
-          sc2 = f2_fma(w, make_float2(ynl[j], ynl[j + 1]), sc2);
+          for (int j = 0; j < HC; j += 2) {
+            const float2 x = f2_fma(make_float2(s[j], s[j + 1]), make_float2(a.c, a.c),
+                                    make_float2(nlse[j], nlse[j + 1]));
+            // p = 2^x <= 1 up to the rounding of x (a few ulps above 1 at most),
+            // which rounding p to bf16 / fp16 maps to 1: the clamp is needed only
+            // when p keeps fp32
+            const float2 pr = ROUND == DROPKV_ROUND_NONE
+                                  ? make_float2(fminf(ex2f(x.x), 1.f), fminf(ex2f(x.y), 1.f))
+                                  : round_p2<ROUND>(make_float2(ex2f(x.x), ex2f(x.y)));
+            const float2 den = f2_add(f2_sub(make_float2(1.f, 1.f), pr), make_float2(p.eps, p.eps));
+            const float2 ratio = f2_mul(pr, make_float2(rcpf(den.x), rcpf(den.y)));
+            const float2 w = f2_mul(ratio, ratio);
+            sw2 = f2_add(sw2, w);
+            sb2 = f2_fma(w, make_float2(s2[j], s2[j + 1]), sb2);
+            sc2 = f2_fma(w, make_float2(ynl[j], ynl[j + 1]), sc2);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < HC; j += 2) {
+            const bool ok0 = edge ? (key <= bnd_s[cbase + j] && key < Lk) : (cbase + j < M);
+            const bool ok1 = edge ? (key <= bnd_s[cbase + j + 1] && key < Lk) : (cbase + j + 1 < M);
+            const float2 x = f2_fma(make_float2(s[j], s[j + 1]), make_float2(a.c, a.c),
+                                    make_float2(nlse[j], nlse[j + 1]));
+            const float2 pr = round_p2<ROUND>(make_float2(fminf(ex2f(x.x), 1.f), fminf(ex2f(x.y), 1.f)));
+            const float2 den = f2_add(f2_sub(make_float2(1.f, 1.f), pr), make_float2(p.eps, p.eps));
+            const float2 ratio = f2_mul(pr, make_float2(rcpf(den.x), rcpf(den.y)));
+            float2 w = f2_mul(ratio, ratio);
+            w.x = ok0 ? w.x : 0.f;
+            w.y = ok1 ? w.y : 0.f;
+            sw2 = f2_add(sw2, w);
+            sb2 = f2_fma(w, make_float2(s2[j], s2[j + 1]), sb2);
+            sc2 = f2_fma(w, make_float2(ynl[j], ynl[j + 1]), sc2);
+          }
         }
         float sw = sw2.x + sw2.y, sb = sb2.x + sb2.y, sc = sc2.x + sc2.y;
         // column groups 1-3 hand their sums to group 0 (fixed order: deterministic)

@@ -266,6 +266,14 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
   return d;
 }
 
+// The descriptor of the same operand `bytes` further on (a multiple of 16): the
+// start address is the low 14-bit field, and shared-memory addresses stay below
+// 256 KB, so the offset is added to the low word without a carry into the rest.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) {
+  const uint32_t lo = (uint32_t)d + (bytes >> 4), hi = (uint32_t)(d >> 32);
+  return ((uint64_t)hi << 32) | lo;
+}
+
 // Instruction descriptor, kind::f16 with fp32 accumulation.
 __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn_major ? 1u : 0u) << 15) |
