@@ -29,6 +29,14 @@ machine (torch.cat storage as in the reference): (i) the last chunk of the
 ``last_chunk`` strategy (every layer evicts its 131072-key cache) and (ii) the
 whole ``every_chunk`` prefill, device-timed with events around the calls.
 
+``--workload qwen2``: config 3 on one GPU -- a random-init Qwen2-0.5B
+(Transformers' Qwen2ForCausalLM, bf16) prefills 8192 seeded random token ids
+with dropkv_b200.hf.DropKVCache (keep_ratio 0.1, eviction through the C ABI at
+every layer) and greedy-decodes 256 tokens over the compressed cache; reports
+the summed eviction time of the 24 layers and decode tokens/s, with decode
+attention by dropkv_decode_attention and, beside it, by Transformers' SDPA
+over the concatenated cache (the reference patch's decode path).
+
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 numpy restatement in oracle/, the reference being Python with no compiled part)
 on the host cores, rank 0 only.
@@ -64,11 +72,15 @@ def parse_args():
     ap.add_argument("--keep-ratio", type=float, default=0.1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["layer", "ragged", "chunked", "decode"], default="layer",
+    ap.add_argument("--workload", choices=["layer", "ragged", "chunked", "decode", "qwen2"], default="layer",
                     help="layer: one Llama layer per rank (default, weak scaling); ragged: the "
                          "config-5 batch split across ranks (strong scaling); chunked: config-4 "
                          "chunked prefill through DropKVCache / prefill_chunked (1 GPU); decode: "
-                         "token steps over 32 compressed Llama layer caches (1 GPU)")
+                         "token steps over 32 compressed Llama layer caches (1 GPU); qwen2: config 3, a "
+                         "random-init Qwen2-0.5B prefilling 8192 tokens through the Transformers "
+                         "integration, then greedy decoding (1 GPU)")
+    ap.add_argument("--prompt", type=int, default=8192, help="qwen2: prompt tokens")
+    ap.add_argument("--new-tokens", type=int, default=256, help="qwen2: greedy decode steps")
     ap.add_argument("--chunked-layers", type=int, default=32)
     ap.add_argument("--chunk", type=int, default=4096)
     ap.add_argument("--storage", choices=["cat", "buffer"], default="cat",
@@ -771,6 +783,84 @@ def run_decode(args):
     print(json.dumps(line), flush=True)
 
 
+QWEN2_METRIC = "config 3: Qwen2-0.5B (random init) greedy decode tokens/s after DropKV prefill eviction of 8192 tokens"
+
+
+def run_qwen2(args):
+    """Config 3 through the Transformers integration (dropkv_b200.hf)."""
+    import torch
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    from dropkv_b200 import _lib, hf
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = Qwen2Config(vocab_size=151936, hidden_size=896, intermediate_size=4864, num_hidden_layers=24,
+                      num_attention_heads=14, num_key_value_heads=2, max_position_embeddings=32768,
+                      rope_theta=1e6, rms_norm_eps=1e-6, tie_word_embeddings=True)
+    torch.manual_seed(11)
+    with torch.device(dev):
+        model = Qwen2ForCausalLM(cfg)
+    model = model.to(torch.bfloat16).eval()
+    hf.enable_query_states(model)
+    hf.register_attention("dropkv")
+    g = torch.Generator().manual_seed(12)
+    ids = torch.randint(0, cfg.vocab_size, (1, args.prompt), generator=g).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def run(attn, new_tokens):
+        model.config._attn_implementation = attn
+        cache = hf.DropKVCache(cfg, keep_ratio=args.keep_ratio, window_size=8, kernel_size=11)
+        cache.record_timing(True)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        toks = []
+        l0 = _lib.launch_count()
+        with torch.no_grad():
+            ev[0].record(stream)
+            out = model(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+            tok = out.logits[:, -1:].argmax(-1)
+            ev[1].record(stream)
+            for _ in range(new_tokens):
+                toks.append(tok)
+                out = model(input_ids=tok, past_key_values=cache, use_cache=True, logits_to_keep=1)
+                tok = out.logits[:, -1:].argmax(-1)
+            ev[2].record(stream)
+        torch.cuda.synchronize(dev)
+        launches = _lib.launch_count() - l0
+        return {"prefill_ms": ev[0].elapsed_time(ev[1]), "decode_ms": ev[1].elapsed_time(ev[2]),
+                "compression_ms": cache.compression_ms(), "tokens": torch.cat(toks, 1).cpu(),
+                "kept": int(cache.layers[0].keys.shape[2]) - new_tokens, "launches": launches}
+
+    for attn in ("dropkv", "sdpa"):  # warm-up: kernels, cuBLAS heuristics, allocator
+        run(attn, 8)
+    clocks = ClockSampler(gpu_uuid(dev))
+    clocks.start()
+    ours = run("dropkv", args.new_tokens)
+    clk = clocks.stop()
+    ref = run("sdpa", args.new_tokens)
+    agree = float((ours["tokens"] == ref["tokens"]).float().mean())
+    tps = args.new_tokens / (ours["decode_ms"] / 1e3)
+    line = {
+        "metric": QWEN2_METRIC, "value": tps, "unit": "tokens/s", "n_gpus": 1, "steps": args.new_tokens,
+        "warmup": 1, "ms_per_step": ours["decode_ms"] / args.new_tokens, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded uniform token ids; random-init weights)",
+        "config": {"workload": "qwen2_0.5b_prefill8192_decode256", "layers": 24, "hidden": 896, "Hq": 14,
+                   "Hkv": 2, "D": 64, "mlp": 4864, "vocab": 151936, "rope_theta": 1e6,
+                   "prompt": args.prompt, "new_tokens": args.new_tokens, "keep_ratio": args.keep_ratio,
+                   "kept_per_layer": ours["kept"], "window": 8, "kernel_size": 11,
+                   "path": "Transformers Qwen2ForCausalLM + dropkv_b200.hf (DropKVCache, query-states "
+                           "plumbing, attn_implementation 'dropkv'), eager per-token forward"},
+        "compression_ms": ours["compression_ms"],
+        "compression_ms_per_layer": ours["compression_ms"] / 24,
+        "prefill_ms": ours["prefill_ms"],
+        "decode_sdpa": {"tokens_per_s": args.new_tokens / (ref["decode_ms"] / 1e3),
+                        "what": "the same cache with Transformers' SDPA over the concatenated K/V "
+                                "(the reference patch's decode path)"},
+        "greedy_token_agreement_vs_sdpa": agree,
+        "cpu_baseline": None, "e2e": None, "gpu_launches": ours["launches"], "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1")) > 1
@@ -779,11 +869,11 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, n)
         return
-    if args.workload in ("chunked", "decode"):
+    if args.workload in ("chunked", "decode", "qwen2"):
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         if rank == 0:
-            (run_chunked if args.workload == "chunked" else run_decode)(args)
+            {"chunked": run_chunked, "decode": run_decode, "qwen2": run_qwen2}[args.workload](args)
         return
     import torch
     import torch.distributed as dist
