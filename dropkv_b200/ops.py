@@ -371,3 +371,67 @@ class Compressor:
                                  self.workspace.numel(), st)
         _lib.check(rc, "dropkv_compress")
         return self.keep_idx, self.k_out, self.v_out
+
+
+class HostPipeline:
+    """Compress a sequence of layers whose Q/K/V live in (pinned) host memory and
+    whose outputs go back to host memory, as for a KV cache offloaded to the host.
+
+    Two device slots, each with its input buffers and a ``Compressor``, and one
+    CUDA stream per stage: the host-to-device copy of layer i + 1 runs while layer
+    i is compressed and its outputs copied back, so the PCIe link stays busy in
+    both directions. Every layer's copies and compression are done; only their
+    order in time overlaps. Host tensors should be pinned for the copies to be
+    asynchronous.
+    """
+
+    def __init__(self, B: int, Hq: int, Hkv: int, Lq: int, Lk: int, D: int, dtype: torch.dtype,
+                 window: int, kernel_size: int, keep_len: int, device="cuda", **kw):
+        self.device = torch.device(device)
+        self.shape = (B, Hq, Hkv, Lq, Lk, D)
+        with torch.cuda.device(self.device):
+            self.comps = [Compressor(B, Hq, Hkv, Lq, Lk, D, dtype, window, kernel_size, keep_len,
+                                     device=self.device, **kw) for _ in range(2)]
+            self.inputs = [(torch.empty(B, Hq, Lq, D, dtype=dtype, device=self.device),
+                            torch.empty(B, Hkv, Lk, D, dtype=dtype, device=self.device),
+                            torch.empty(B, Hkv, Lk, D, dtype=dtype, device=self.device)) for _ in range(2)]
+            self.h2d = torch.cuda.Stream(self.device)
+            self.work = torch.cuda.Stream(self.device)
+            self.d2h = torch.cuda.Stream(self.device)
+        self.loaded = [torch.cuda.Event() for _ in range(2)]
+        self.computed = [torch.cuda.Event() for _ in range(2)]
+        self.returned = [torch.cuda.Event() for _ in range(2)]
+        self.used = [False, False]
+
+    def run(self, layers):
+        """``layers``: iterable of (Qh, Kh, Vh, idx_out, kc_out, vc_out) host tensors;
+        inputs [B,Hq,Lq,D] / [B,Hkv,Lk,D], outputs [B,Hkv,keep_len] int64 and
+        [B,Hkv,keep_len,D]. Enqueues everything and returns the event that
+        completes when the last output has reached the host (the caller
+        synchronises on it before reading the outputs)."""
+        last = None
+        for i, (Qh, Kh, Vh, idx_o, kc_o, vc_o) in enumerate(layers):
+            s = i % 2
+            Qd, Kd, Vd = self.inputs[s]
+            comp = self.comps[s]
+            with torch.cuda.stream(self.h2d):
+                if self.used[s]:  # the slot's inputs were read by its previous compression
+                    self.h2d.wait_event(self.computed[s])
+                Qd.copy_(Qh, non_blocking=True)
+                Kd.copy_(Kh, non_blocking=True)
+                Vd.copy_(Vh, non_blocking=True)
+                self.loaded[s].record(self.h2d)
+            self.work.wait_event(self.loaded[s])
+            if self.used[s]:  # the slot's outputs were copied out
+                self.work.wait_event(self.returned[s])
+            comp.run(Qd, Kd, Vd, stream=self.work.cuda_stream)
+            self.computed[s].record(self.work)
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self.computed[s])
+                idx_o.copy_(comp.keep_idx, non_blocking=True)
+                kc_o.copy_(comp.k_out, non_blocking=True)
+                vc_o.copy_(comp.v_out, non_blocking=True)
+                self.returned[s].record(self.d2h)
+            self.used[s] = True
+            last = self.returned[s]
+        return last
