@@ -8,13 +8,18 @@ Public API (the reference's names and semantics):
 * ``DropKVCache(keep_ratio=0.1, window_size=8, kernel_size=11, use_triton=True)``
   and ``prefill_chunked(model, input_ids, cache, ...)``.
 * ``compress`` / ``scores`` / ``select_keep_indices`` / ``gather_compressed``:
-  the stages as tensor functions over the C ABI (include/dropkv_b200.h).
+  the stages as tensor functions over the C ABI (include/dropkv_b200.h);
+  ``Compressor`` (pre-planned, allocation-free calls) and ``HostPipeline``
+  (host-resident layers with overlapped copies).
+* ``dropkv_b200.hf`` (imported on demand, needs transformers): the
+  Transformers integration -- ``DropKVCache(config, ...)``, query-state
+  plumbing, decode attention over the compressed cache, generate wiring.
 """
 
 from ._lib import DropKVError, version
 from .cache import Cache, DropKVCache, DynamicCache, prefill_chunked
-from .ops import (compress, decode_attention, dropkv_scores_cuda, gather_compressed, scores,
-                  select_keep_indices)
+from .ops import (Compressor, HostPipeline, compress, decode_attention, dropkv_scores_cuda,
+                  gather_compressed, scores, select_keep_indices)
 
 # Name of the reference entry point (dropkv_triton.py:643) for drop-in imports.
 dropkv_scores_triton = dropkv_scores_cuda
@@ -22,5 +27,5 @@ dropkv_scores_triton = dropkv_scores_cuda
 __all__ = [
     "Cache", "DynamicCache", "DropKVCache", "prefill_chunked", "DropKVError", "version",
     "compress", "decode_attention", "dropkv_scores_cuda", "dropkv_scores_triton", "gather_compressed",
-    "scores", "select_keep_indices",
+    "scores", "select_keep_indices", "Compressor", "HostPipeline",
 ]
