@@ -72,6 +72,9 @@ def parse_args():
     ap.add_argument("--keep-ratio", type=float, default=0.1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--phases", action="store_true",
+                    help="layer workload: add the scorer's in-kernel phase trace (per round, median over "
+                         "CTAs, microseconds) to the JSON line")
     ap.add_argument("--workload", choices=["layer", "ragged", "chunked", "decode", "qwen2"], default="layer",
                     help="layer: one Llama layer per rank (default, weak scaling); ragged: the "
                          "config-5 batch split across ranks (strong scaling); chunked: config-4 "
@@ -337,6 +340,11 @@ def run_ours(args, rank, n, world):
         except Exception:
             traffic = None
 
+    phases = None
+    if args.phases:
+        from dropkv_b200.diagnostics import scorer_phases
+        phases = scorer_phases(Q, K, V, wl.window_size)
+
     # ---- end to end through the C ABI with host buffers ---------------------
     e2e = None
     if not args.no_e2e:
@@ -399,6 +407,8 @@ def run_ours(args, rank, n, world):
             "step_ms_min_max": [min(step_ms), max(step_ms)],
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
         }
+        if phases is not None:
+            line["scorer_phases_us"] = phases
         print(json.dumps(line), flush=True)
 
 

@@ -213,3 +213,28 @@ def test_buffer_storage_non_evicting_paths_on_cpu(storage):
     assert torch.equal(c.key_cache[0], torch.cat([K[:, :, :30], K[:, :, :1]], dim=2))
     with pytest.raises(ValueError):
         DropKVCache(storage="ring")
+
+
+def test_phase_table_from_synthetic_trace():
+    """The scorer's phase-trace reader: header, layout and per-round medians."""
+    import torch
+    from dropkv_b200 import diagnostics as dg
+    ctas, rounds, nev = 3, 2, 9
+    stamps = torch.zeros(ctas, rounds, nev, dtype=torch.int64)
+    for c in range(ctas):
+        for r in range(rounds):
+            base = 1_000_000 + r * 50_000 + c * 100
+            stamps[c, r] = base + torch.arange(nev) * (1000 * (c + 1))  # phases of 1, 2, 3 us
+    off = 256
+    ws = torch.zeros(off + 256 + 8 * (3 + stamps.numel()), dtype=torch.uint8)
+    tr = ws[off + 256:].view(torch.int64)
+    tr[:3] = torch.tensor([ctas, rounds, nev])
+    tr[3:] = stamps.flatten()
+    t = dg.read_trace(ws, off)
+    rows = dg.phase_table(t)
+    assert len(rows) == 2 and set(dg.PHASES) <= set(rows[0])
+    assert all(abs(rows[r][p] - 2.0) < 1e-9 for r in range(2) for p in dg.PHASES)  # median of 1, 2, 3
+    assert abs(rows[1]["start_us"] - 50.1) < 1e-9
+    bad = torch.zeros(1024, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="no scorer trace"):
+        dg.read_trace(bad, 256)
