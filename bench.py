@@ -17,7 +17,8 @@ max over ranks of the device-timed region.
 
 ``--workload ragged``: the config-5 batch (16 sequences, Lk drawn uniformly
 from [4096, 65536], 32 Llama layers each), split across ranks by
-(sequence, layer) units balanced longest-first (dropkv_b200.sharding); every
+(sequence, layer) units cut into consecutive runs of equal work (or balanced
+longest-first, ``--ragged-partition lpt``; dropkv_b200.sharding); every
 rank generates and runs only its own units, no collective on the data path;
 value = all units' positions / max over ranks of the device time (strong
 scaling: the total work is fixed).
@@ -91,6 +92,9 @@ def parse_args():
     ap.add_argument("--ragged-seqs", type=int, default=16)
     ap.add_argument("--ragged-layers", type=int, default=32)
     ap.add_argument("--ragged-seed", type=int, default=5)
+    ap.add_argument("--ragged-partition", choices=["contiguous", "lpt"], default="contiguous",
+                    help="ragged: units cut into consecutive (sequence, layer) runs of equal work, or "
+                         "longest-first to the least loaded rank (dropkv_b200.sharding)")
     ap.add_argument("--ragged-batch", choices=["sequence", "unit"], default="sequence",
                     help="ragged: one compress call per sequence over the rank's layers of it "
                          "(B = layers), or one call per (sequence, layer) unit")
@@ -422,13 +426,13 @@ def run_ragged(args, rank, n, world):
     import torch
     import torch.distributed as dist
     from dropkv_b200 import _lib, ops
-    from dropkv_b200.sharding import load_imbalance, lpt_partition, make_units, ragged_lengths
+    from dropkv_b200.sharding import PARTITIONS, load_imbalance, make_units, ragged_lengths
     from dropkv_b200.workloads import llama_layer, make_qkv
 
     dev = torch.device("cuda", torch.cuda.current_device())
     lengths = ragged_lengths(args.ragged_seqs, 4096, 65536, args.ragged_seed)
     all_units = make_units(lengths, args.ragged_layers)
-    parts = lpt_partition(all_units, n)
+    parts = PARTITIONS[args.ragged_partition](all_units, n)
     mine = parts[rank]
     comps, work = {}, []
     if args.ragged_batch == "unit":
@@ -512,7 +516,9 @@ def run_ragged(args, rank, n, world):
                    "units": len(all_units), "units_per_rank": [len(p) for p in parts],
                    "calls_per_pass_rank0": len(work), "batching": args.ragged_batch,
                    "load_imbalance": load_imbalance(parts),
-                   "parallelism": f"{n} ranks, (sequence, layer) units, longest-first balance, no collective",
+                   "partition": args.ragged_partition,
+                   "parallelism": f"{n} ranks, (sequence, layer) units, {args.ragged_partition} partition, "
+                                  "no collective",
                    "l2": "distinct inputs per unit, whole batch far above the 126 MB L2"},
         "roofline": {"bound": "hbm", "achieved": per_gpu_gbs, "peak": peak, "unit": "GB/s",
                      "frac": per_gpu_gbs / peak, "traffic": None,

@@ -11,6 +11,10 @@ A unit here is one (sequence, layer) pair: all KV heads of that layer of that
 sequence, i.e. one ``dropkv_compress`` call of B = 1.  Its cost is proportional to
 its key count Lk (K and V are streamed once), so units are balanced by
 longest-processing-time-first: the heaviest unit goes to the least loaded rank.
+That spreads every sequence over all ranks, though, and a rank makes one call
+per sequence it holds; ``contiguous_partition`` instead cuts the units, in
+(sequence, layer) order, into runs of nearly equal work, so a rank holds whole
+layer ranges of a few sequences and makes a few large calls.
 """
 
 from __future__ import annotations
@@ -54,11 +58,33 @@ def lpt_partition(units: list[Unit], n_ranks: int) -> list[list[Unit]]:
     return parts
 
 
-def rank_plan(rank: int, n_ranks: int, lengths: list[int], layers: int) -> list[Unit]:
+def contiguous_partition(units: list[Unit], n_ranks: int) -> list[list[Unit]]:
+    """Units in (sequence, layer) order cut into ``n_ranks`` consecutive runs: a
+    unit goes to the next rank once the work before its midpoint passes that
+    rank's share, so each rank's load is within half a unit of an equal split at
+    both of its ends. Deterministic; every unit is placed once."""
+    if n_ranks < 1:
+        raise ValueError("n_ranks must be >= 1")
+    order = sorted(units, key=lambda u: (u.seq, u.layer))
+    total = sum(u.lk for u in order)
+    parts: list[list[Unit]] = [[] for _ in range(n_ranks)]
+    acc, r = 0, 0
+    for u in order:
+        while r < n_ranks - 1 and 2 * acc + u.lk > 2 * (r + 1) * total / n_ranks:
+            r += 1
+        parts[r].append(u)
+        acc += u.lk
+    return parts
+
+
+PARTITIONS = {"lpt": lpt_partition, "contiguous": contiguous_partition}
+
+
+def rank_plan(rank: int, n_ranks: int, lengths: list[int], layers: int, method: str = "lpt") -> list[Unit]:
     """The units rank ``rank`` of ``n_ranks`` runs."""
     if not 0 <= rank < n_ranks:
         raise ValueError(f"rank {rank} outside [0, {n_ranks})")
-    return lpt_partition(make_units(lengths, layers), n_ranks)[rank]
+    return PARTITIONS[method](make_units(lengths, layers), n_ranks)[rank]
 
 
 def load_imbalance(parts: list[list[Unit]]) -> float:
