@@ -73,6 +73,8 @@ def parse_args():
     ap.add_argument("--keep-ratio", type=float, default=0.1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="layer workload: time call-by-call dropkv_compress instead of its CUDA-graph replay")
     ap.add_argument("--phases", action="store_true",
                     help="layer workload: add the scorer's in-kernel phase trace (per round, median over "
                          "CTAs, microseconds) to the JSON line")
@@ -286,6 +288,21 @@ def run_ours(args, rank, n, world):
     for _ in range(args.warmup):
         comp.run(Q, K, V)
     barrier()
+    # the same steps issued call by call (reported beside the graph figure)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        comp.run(Q, K, V)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    eager_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    # the timed steps: one dropkv_compress call captured once in a CUDA graph and
+    # replayed (every step launches the scorer, selection and gather again)
+    per_graph = comp.capture(Q, K, V) if not args.no_graph else 0
+    step = comp.replay if per_graph else (lambda: comp.run(Q, K, V))
+    for _ in range(args.warmup):
+        step()
+    barrier()
     clocks = ClockSampler(gpu_uuid(dev))
     clocks.start()
     time.sleep(0.3)
@@ -293,10 +310,10 @@ def run_ours(args, rank, n, world):
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     ev[0].record(stream)
     for i in range(args.steps):
-        comp.run(Q, K, V)
+        step()
         ev[i + 1].record(stream)
     torch.cuda.synchronize(dev)
-    launches = _lib.launch_count() - n_launch0
+    launches = (_lib.launch_count() - n_launch0) + per_graph * args.steps
     clk = clocks.stop()
     total_ms = ev[0].elapsed_time(ev[-1])
     step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
@@ -409,6 +426,9 @@ def run_ours(args, rank, n, world):
                               "frac": path_gbs / peak, "algorithmic_bytes": path_bytes,
                               "ms": ms_per_step},
             "step_ms_min_max": [min(step_ms), max(step_ms)],
+            "step": ("one dropkv_compress call (scorer, selection, gather) replayed from a CUDA graph"
+                     if per_graph else "one dropkv_compress call"),
+            "eager_ms_per_step": eager_ms,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
         }
         if phases is not None:

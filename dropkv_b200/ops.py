@@ -372,6 +372,29 @@ class Compressor:
         _lib.check(rc, "dropkv_compress")
         return self.keep_idx, self.k_out, self.v_out
 
+    def capture(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor) -> int:
+        """Capture one ``run`` on these (fixed-address) inputs into a CUDA graph that
+        ``replay`` launches again: the same kernels and copies, without the host's
+        per-call work. Returns the number of kernel launches in the graph."""
+        cur = torch.cuda.current_stream(self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            self.run(Q, K, V)  # first use of every kernel and launch attribute off the capture
+        cur.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        n0 = _lib.launch_count()
+        with torch.cuda.graph(graph):
+            self.run(Q, K, V)
+        self.graph = graph
+        self.graph_launches = _lib.launch_count() - n0
+        return self.graph_launches
+
+    def replay(self):
+        """Launch the graph ``capture`` recorded (on the current stream)."""
+        self.graph.replay()
+        return self.keep_idx, self.k_out, self.v_out
+
 
 class HostPipeline:
     """Compress a sequence of layers whose Q/K/V live in (pinned) host memory and

@@ -29,3 +29,19 @@ def test_host_pipeline_matches_per_layer_compress():
             assert torch.equal(item[3], idx.cpu())
             assert torch.equal(item[4], kc.cpu())
             assert torch.equal(item[5], vc.cpu())
+
+
+def test_compressor_graph_replay_matches_run():
+    dev = torch.device("cuda")
+    wl = llama_layer(32768, seed=6)
+    Q, K, V = make_qkv(wl, dev)
+    kl = wl.keep_len()
+    comp = ops.Compressor(1, 32, 8, 8, 32768, 128, torch.bfloat16, 8, 11, kl, device=dev)
+    idx, kc, vc = (t.clone() for t in comp.run(Q, K, V))
+    assert comp.capture(Q, K, V) >= 3  # scorer, selection, gather
+    for t in (comp.keep_idx, comp.k_out, comp.v_out):
+        t.zero_()
+    for _ in range(2):
+        comp.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(comp.keep_idx, idx) and torch.equal(comp.k_out, kc) and torch.equal(comp.v_out, vc)
