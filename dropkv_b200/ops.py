@@ -457,4 +457,7 @@ class HostPipeline:
                 self.returned[s].record(self.d2h)
             self.used[s] = True
             last = self.returned[s]
+        if last is None:  # nothing enqueued: an event that completes at once
+            last = torch.cuda.Event()
+            last.record(self.d2h)
         return last
