@@ -384,7 +384,9 @@ class Compressor:
         cur.wait_stream(side)
         graph = torch.cuda.CUDAGraph()
         n0 = _lib.launch_count()
-        with torch.cuda.graph(graph):
+        # thread_local: CUDA calls other threads make meanwhile (a communication
+        # library's watchdog, say) do not invalidate this capture
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
             self.run(Q, K, V)
         self.graph = graph
         self.graph_launches = _lib.launch_count() - n0
