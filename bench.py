@@ -11,9 +11,13 @@ scores, pools, selects and compacts the whole layer (dropkv_compress, one C-ABI
 call).  Metric: KV positions scored+compacted per second, one position = one
 (sequence, KV head, key position).
 
-Multi-GPU (torchrun, one rank per GPU): every rank processes its own layer
-(weak scaling, no collective on the data path); value = all ranks' positions /
-max over ranks of the device-timed region.
+Multi-GPU (torchrun, one rank per GPU): the layer's 8 KV heads are split
+across the ranks (sequence, KV head units; strong scaling, no collective on the
+data path); value = the layer's positions / max over ranks of the device-timed
+region.  The line also carries, at every N, the config-5 ragged batch at
+keep_ratio 0.1 / 0.25 / 0.5 (``ragged``), and at N = 1 the reference's own CPU
+path (``cpu_baseline``) and its Triton GPU path timed on the same GPU
+(``gpu_bar``).
 
 ``--workload ragged``: the config-5 batch (16 sequences, Lk drawn uniformly
 from [4096, 65536], 32 Llama layers each), split across ranks by
@@ -38,9 +42,10 @@ the summed eviction time of the 24 layers and decode tokens/s, with decode
 attention by dropkv_decode_attention and, beside it, by Transformers' SDPA
 over the concatenated cache (the reference patch's decode path).
 
-``--impl reference`` times the reference algorithm's CPU implementation (the
-numpy restatement in oracle/, the reference being Python with no compiled part)
-on the host cores, rank 0 only.
+``--impl reference`` times the reference's own CPU path (DropKVCache with
+use_triton=False + _gather_compressed, installed unmodified into baseline/_ref
+by pip) on the host cores, rank 0 only; the numpy port (oracle/) is timed beside
+it as ``port_baseline``.
 """
 
 from __future__ import annotations
@@ -73,6 +78,12 @@ def parse_args():
     ap.add_argument("--keep-ratio", type=float, default=0.1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-bar", action="store_true",
+                    help="layer workload: skip timing the reference's Triton path on this GPU")
+    ap.add_argument("--no-ragged", action="store_true",
+                    help="layer workload: skip the nested config-5 ragged record")
+    ap.add_argument("--gpu-bar-only", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--bar-idx", default="", help=argparse.SUPPRESS)
     ap.add_argument("--no-graph", action="store_true",
                     help="layer workload: time call-by-call dropkv_compress instead of its CUDA-graph replay")
     ap.add_argument("--phases", action="store_true",
@@ -197,21 +208,73 @@ def gpu_uuid(dev):
 
 
 # ---------------------------------------------------------------------------
-# reference arm (CPU)
+# the reference (installed unmodified into baseline/_ref) and the numpy port
 # ---------------------------------------------------------------------------
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 _CPU_INPUTS = {}
 
 
-def cpu_oracle_rate(wl, heads: int):
-    """Time the oracle (numpy) on `heads` KV heads of the workload; positions/s."""
+def reference_modules():
+    """(dropkv_cache, dropkv_triton) of the reference as pip installed it into
+    baseline/_ref (its own public modules, unmodified), or (None, reason)."""
+    if not os.path.isfile(os.path.join(REF_DIR, "dropkv_cache.py")):
+        return None, "the reference is not installed in baseline/_ref"
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        import dropkv_cache  # noqa: F401  (reference module)
+        import dropkv_triton  # noqa: F401  (reference module)
+    except Exception as e:  # pragma: no cover - depends on the box
+        return None, f"import of the reference failed: {type(e).__name__}: {e}"
+    return (dropkv_cache, dropkv_triton), None
+
+
+def reference_step(mods, wl, Q, K, V, use_triton: bool):
+    """The reference's eviction path through its public API: DropKVCache
+    ._compute_keep_indices then _gather_compressed (dropkv_cache.py:355-491)."""
+    dropkv_cache = mods[0]
+    cache = dropkv_cache.DropKVCache(keep_ratio=wl.keep_ratio, window_size=wl.window_size,
+                                     kernel_size=wl.kernel_size, use_triton=use_triton)
+    idx = cache._compute_keep_indices(Q, K, V)
+    kc, vc = dropkv_cache.DropKVCache._gather_compressed(K, V, idx)
+    return idx, kc, vc
+
+
+def cpu_inputs(wl, heads: int):
+    """CPU (bf16) inputs of the workload's first ``heads`` KV heads (cached)."""
     from dropkv_b200.workloads import make_qkv
-    from oracle import dropkv_oracle as O
     key = (wl, heads)
     if key not in _CPU_INPUTS:
         Q, K, V = make_qkv(wl, "cpu")
-        _CPU_INPUTS[key] = (Q[:, :heads * wl.g].float().numpy(), K[:, :heads].float().numpy(),
-                            V[:, :heads].float().numpy())
-    Qn, Kn, Vn = _CPU_INPUTS[key]
+        _CPU_INPUTS[key] = (Q[:, :heads * wl.g].contiguous(), K[:, :heads].contiguous(), V[:, :heads].contiguous())
+    return _CPU_INPUTS[key]
+
+
+def reference_cpu_rate(wl, heads: int, reps: int = 1):
+    """Time the reference's own CPU path (torch, all host threads) on ``heads`` KV
+    heads of the workload: (positions/s, seconds per run, threads) or None."""
+    import torch
+    mods, why = reference_modules()
+    if mods is None:
+        return None, why
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    Q, K, V = cpu_inputs(wl, heads)
+    reference_step(mods, wl, Q, K, V, False)  # warm-up (allocator, thread pool)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        reference_step(mods, wl, Q, K, V, False)
+        ts.append(time.perf_counter() - t0)
+    dt = statistics.median(ts)
+    return (wl.B * heads * wl.Lk / dt, dt, threads), None
+
+
+def cpu_oracle_rate(wl, heads: int):
+    """Time the numpy port (oracle.compress) on ``heads`` KV heads; positions/s."""
+    from oracle import dropkv_oracle as O
+    Q, K, V = cpu_inputs(wl, heads)
+    Qn, Kn, Vn = Q.float().numpy(), K.float().numpy(), V.float().numpy()
     t0 = time.perf_counter()
     O.compress(Qn, Kn, Vn, wl.window_size, wl.kernel_size, wl.keep_ratio, round_p="bf16")
     dt = time.perf_counter() - t0
@@ -228,49 +291,170 @@ def blas_threads():
         return os.cpu_count() or 1
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def run_reference(args, rank, n):
+    """``--impl reference``: the reference's own CPU path (DropKVCache with
+    use_triton=False, then _gather_compressed; torch bf16 on all host threads) on
+    this arm's workload, rank 0 only. Each step is the whole layer unless that
+    would take the run past a few minutes; then a step is the first heads of it."""
     if rank != 0:
         return
+    import torch
     wl = workload(args)
+    mods, why = reference_modules()
+    if mods is None:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     heads = wl.Hkv
-    rates = []
+    Q, K, V = cpu_inputs(wl, heads)
+    t0 = time.perf_counter()
+    reference_step(mods, wl, Q, K, V, False)
+    t_layer = time.perf_counter() - t0
+    budget_s = 150.0
+    if (args.warmup + args.steps) * t_layer > budget_s:
+        heads = max(1, int(wl.Hkv * budget_s / ((args.warmup + args.steps) * t_layer)))
+        Q, K, V = cpu_inputs(wl, heads)
+    ts = []
     for i in range(args.warmup + args.steps):
-        r, _ = cpu_oracle_rate(wl, heads)
+        t0 = time.perf_counter()
+        reference_step(mods, wl, Q, K, V, False)
         if i >= args.warmup:
-            rates.append(r)
-    ms = [wl.B * heads * wl.Lk / r * 1e3 for r in rates]
-    value = len(rates) * wl.B * heads * wl.Lk / (sum(ms) / 1e3)
-    cores = blas_threads()
-    sample = (f"oracle.compress (numpy fp32; BLAS {cores} threads, elementwise 1 thread) over "
-              f"{heads} KV heads x Lk={wl.Lk} per step")
+            ts.append(time.perf_counter() - t0)
+    per_step_pos = wl.B * heads * wl.Lk
+    value = len(ts) * per_step_pos / sum(ts)
+    sample = (f"reference DropKVCache(use_triton=False)._compute_keep_indices + _gather_compressed "
+              f"(baseline/_ref, torch {torch.__version__} bf16 on CPU, {threads} threads, {cpu_model()}) over "
+              f"{heads} of {wl.Hkv} KV heads x Lk={wl.Lk} per step")
+    port_rate, port_dt = cpu_oracle_rate(wl, 1)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(ms),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded)", "config": config_of(wl, 1),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": statistics.mean(ts) * 1e3 * wl.Hkv / heads,
+        "higher_is_better": True, "scaling": "strong" if n > 1 else "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded)", "config": config_of(wl, n),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
+        "port_baseline": {"value": port_rate, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+                          "sample": f"oracle.compress (numpy fp32) over 1 KV head, {port_dt:.2f} s"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-# ---------------------------------------------------------------------------
-# our arm
-# ---------------------------------------------------------------------------
+def run_gpu_bar(args):
+    """``--gpu-bar-only``: the reference's GPU path (DropKVCache(use_triton=True):
+    its Triton scorer, then torch max_pool1d / topk / sort / gather) timed with
+    CUDA events on this workload; prints one JSON object. Run by the layer arm in a
+    child process, so that a failure there cannot take the arm's own line down.
+    With ``--bar-idx PATH`` the last step's keep indices are saved there."""
+    import torch
+    from dropkv_b200.workloads import make_qkv
+    mods, why = reference_modules()
+    if mods is None:
+        print(json.dumps({"unavailable": why}), flush=True)
+        return
+    dropkv_triton = mods[1]
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    wl = workload(args)
+    Q, K, V = make_qkv(wl, dev)
+    # the cache would fall back to its PyTorch branch on ImportError/AssertionError:
+    # call the Triton scorer once directly so that a fallback cannot pass for it
+    dropkv_triton.dropkv_scores_triton(Q, K, V, window_size=wl.window_size)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, k):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            out = fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / k, out
+
+    path = lambda: reference_step(mods, wl, Q, K, V, True)  # noqa: E731
+    scorer = lambda: dropkv_triton.dropkv_scores_triton(Q, K, V, window_size=wl.window_size)  # noqa: E731
+    for _ in range(max(3, args.warmup)):
+        path()
+    torch.cuda.synchronize(dev)
+    k = max(3, min(args.steps, 10))
+    path_ms, (idx, _, _) = timed(path, k)
+    score_ms, _ = timed(scorer, k)
+    if args.bar_idx:
+        import numpy as np
+        np.save(args.bar_idx, idx.cpu().numpy())
+    pos = wl.positions
+    print(json.dumps({
+        "ms_per_step": path_ms, "value": pos / (path_ms / 1e3), "unit": UNIT,
+        "scorer_ms": score_ms, "steps": k,
+        "what": "reference DropKVCache(use_triton=True)._compute_keep_indices + _gather_compressed "
+                "(dropkv_scores_triton, then torch max_pool1d/topk/sort/gather) on this GPU, "
+                "CUDA-event time per step; scorer_ms: dropkv_scores_triton alone",
+        "triton": __import__("triton").__version__}), flush=True)
+
+
+def gpu_bar_child(args, dev):
+    """Run ``run_gpu_bar`` in a child process on this rank's GPU; its JSON, with
+    the kept-set agreement against ``ours_idx`` when given, or an error record."""
+    import tempfile
+    cmd = [sys.executable, os.path.abspath(__file__), "--gpu-bar-only", "--lk", str(args.lk),
+           "--keep-ratio", str(args.keep_ratio), "--steps", str(args.steps), "--warmup", str(args.warmup)]
+    env = dict(os.environ)
+    env["CUDA_VISIBLE_DEVICES"] = str(dev.index if dev.index is not None else 0)
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "bar_idx.npy")
+        try:
+            r = subprocess.run(cmd + ["--bar-idx", path], capture_output=True, text=True, timeout=600, env=env)
+        except subprocess.TimeoutExpired:
+            return {"unavailable": "the reference's GPU path did not finish within 600 s"}, None
+        lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+        if r.returncode != 0 or not lines:
+            tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+            return {"unavailable": f"the reference's GPU path failed (exit {r.returncode}): {tail[0][:200]}"}, None
+        bar = json.loads(lines[-1])
+        idx = None
+        if os.path.exists(path):
+            import numpy as np
+            idx = np.load(path)
+        return bar, idx
+
+
 def run_ours(args, rank, n, world):
+    """The layer workload. One step = one dropkv_compress call over this rank's KV
+    heads of the 128K-token Llama layer (all 8 at N = 1; at N > 1 the layer's heads
+    are split across the ranks, strong scaling: the total work is fixed)."""
+    import numpy as np
     import torch
     import torch.distributed as dist
     from dropkv_b200 import _lib, ops
+    from dropkv_b200.sharding import head_range
     from dropkv_b200.workloads import make_qkv
 
     dev = torch.device("cuda", torch.cuda.current_device())
     wl = workload(args)
-    wl_rank = dataclasses.replace(wl, seed=wl.seed + rank)
-    Q, K, V = make_qkv(wl_rank, dev)
+    g = wl.g
+    h0, h1 = head_range(rank, n, wl.Hkv)
+    nh = h1 - h0
+    Qf, Kf, Vf = make_qkv(wl, dev)  # the same layer at every N; this rank scores heads [h0, h1)
+    Q, K, V = Qf[:, h0 * g:h1 * g], Kf[:, h0:h1], Vf[:, h0:h1]
     kl = wl.keep_len()
-    comp = ops.Compressor(wl.B, wl.Hq, wl.Hkv, wl.Lq, wl.Lk, wl.D, wl.dtype, wl.window_size,
-                          wl.kernel_size, kl, device=dev)
+    comp = ops.Compressor(wl.B, nh * g, nh, wl.Lq, wl.Lk, wl.D, wl.dtype, wl.window_size,
+                          wl.kernel_size, kl, device=dev) if nh else None
     stream = torch.cuda.current_stream(dev)
+    lib = _lib.load()
 
     def barrier():
         if world:
@@ -284,29 +468,38 @@ def run_ours(args, rank, n, world):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def gather_ranks(x: float) -> list:
+        if not world:
+            return [x]
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        out = [torch.zeros_like(t) for _ in range(n)]
+        dist.all_gather(out, t)
+        return [float(o.item()) for o in out]
+
+    run = (lambda: comp.run(Q, K, V)) if comp else (lambda: None)
     # ---- device-resident timed region -------------------------------------
     for _ in range(args.warmup):
-        comp.run(Q, K, V)
+        run()
     barrier()
     # the same steps issued call by call (reported beside the graph figure)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        comp.run(Q, K, V)
+        run()
     e1.record(stream)
     torch.cuda.synchronize(dev)
     eager_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     # the timed steps: one dropkv_compress call captured once in a CUDA graph and
     # replayed (every step launches the scorer, selection and gather again)
     per_graph = 0
-    if not args.no_graph:
+    if not args.no_graph and comp:
         try:
             per_graph = comp.capture(Q, K, V)
         except RuntimeError as e:  # capture refused here: time the calls one by one
             print(f"[bench] CUDA graph capture failed ({str(e)[:120]}); timing call by call", file=sys.stderr)
             torch.cuda.synchronize(dev)
             per_graph = 0
-    step = comp.replay if per_graph else (lambda: comp.run(Q, K, V))
+    step = comp.replay if per_graph else run
     for _ in range(args.warmup):
         step()
     barrier()
@@ -324,44 +517,61 @@ def run_ours(args, rank, n, world):
     clk = clocks.stop()
     total_ms = ev[0].elapsed_time(ev[-1])
     step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    rank_ms = gather_ranks(total_ms / args.steps)
     total_ms = max_over_ranks(total_ms)
     ms_per_step = total_ms / args.steps
-    positions = wl.B * wl.Hkv * wl.Lk
-    value = n * positions * args.steps / (total_ms / 1e3)
+    positions = wl.positions  # the whole layer, over all ranks
+    value = positions * args.steps / (total_ms / 1e3)
+
+    # ---- the timed steps did their work: status word clear, outputs as an eager call
+    if comp:
+        dt_code = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16}[wl.dtype]
+        off = lib.dropkv_scores_status_offset(dt_code, wl.B, nh * g, nh, wl.Lk, wl.D, wl.window_size)
+        if off != _lib.NO_STATUS:
+            st = int(comp.workspace[off:off + 4].view(torch.int32).item())
+            if st != 0:
+                raise RuntimeError(f"scorer status word {st} after the timed steps: a bounded wait timed out")
+        idx_e, kc_e, vc_e = ops.compress(Q, K, V, wl.window_size, wl.kernel_size, kl)
+        if not (torch.equal(idx_e, comp.keep_idx) and torch.equal(kc_e, comp.k_out) and torch.equal(vc_e, comp.v_out)):
+            raise RuntimeError("the timed steps' outputs differ from an eager dropkv_compress on the same inputs")
+        del kc_e, vc_e
+    checked = "status word 0 and outputs equal to an eager dropkv_compress after the timed steps"
 
     peak, peak_kind = measured_peaks()
     path_bytes = wl.algorithmic_bytes()
-    path_gbs = path_bytes / (ms_per_step / 1e3) / 1e9
+    path_gbs = path_bytes / (ms_per_step / 1e3) / 1e9 / max(1, min(n, wl.Hkv))
 
-    # ---- per-stage timing (dominant kernel sequence: scoring) --------------
-    sc_ws = torch.empty(_lib.load().dropkv_scores_workspace_size(wl.B, wl.Hq, wl.Hkv, wl.Lk, wl.D, wl.window_size),
-                        dtype=torch.uint8, device=dev)
-    sc_out = torch.empty(wl.B, wl.Hkv, wl.Lk, dtype=torch.float32, device=dev)
-    lib = _lib.load()
+    # ---- per-stage timing (dominant kernel: the scorer) on this rank's heads --
+    score_ms, score_bytes, score_gbs = None, 0, 0.0
+    if comp:
+        sc_ws = torch.empty(lib.dropkv_scores_workspace_size(wl.B, nh * g, nh, wl.Lk, wl.D, wl.window_size),
+                            dtype=torch.uint8, device=dev)
+        sc_out = torch.empty(wl.B, nh, wl.Lk, dtype=torch.float32, device=dev)
 
-    def run_scores():
-        rc = lib.dropkv_scores(Q.data_ptr(), *Q.stride(), wl.Lq, K.data_ptr(), V.data_ptr(), 2,
-                               wl.B, wl.Hq, wl.Hkv, wl.Lk, wl.D, wl.window_size, 1e-6, 1,
-                               sc_out.data_ptr(), sc_ws.data_ptr(), sc_ws.numel(), stream.cuda_stream)
-        _lib.check(rc, "dropkv_scores")
+        def run_scores():
+            rc = lib.dropkv_scores(Q.data_ptr(), *Q.stride(), wl.Lq, K.data_ptr(), V.data_ptr(), 2,
+                                   wl.B, nh * g, nh, wl.Lk, wl.D, wl.window_size, 1e-6, 1,
+                                   sc_out.data_ptr(), sc_ws.data_ptr(), sc_ws.numel(), stream.cuda_stream)
+            _lib.check(rc, "dropkv_scores")
 
-    for _ in range(3):
-        run_scores()
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        run_scores()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    score_ms = e0.elapsed_time(e1) / args.steps
-    e = K.element_size()
-    score_bytes = wl.B * wl.Hkv * (2 * wl.Lk * wl.D * e + wl.g * wl.window_size * wl.D * e + 4 * wl.Lk)
-    score_gbs = score_bytes / (score_ms / 1e3) / 1e9
+        for _ in range(3):
+            run_scores()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            run_scores()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        score_ms = e0.elapsed_time(e1) / args.steps
+        e = K.element_size()
+        score_bytes = wl.B * nh * (2 * wl.Lk * wl.D * e + g * wl.window_size * wl.D * e + 4 * wl.Lk)
+        score_gbs = score_bytes / (score_ms / 1e3) / 1e9
+        del sc_ws, sc_out
 
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
+    if os.path.exists(tp) and nh == wl.Hkv:
         try:
             with open(tp) as f:
                 traffic = json.load(f).get(f"scores_lk{wl.Lk}")
@@ -369,74 +579,108 @@ def run_ours(args, rank, n, world):
             traffic = None
 
     phases = None
-    if args.phases:
+    if args.phases and comp:
         from dropkv_b200.diagnostics import scorer_phases
         phases = scorer_phases(Q, K, V, wl.window_size)
 
     # ---- end to end through the C ABI with host buffers ---------------------
     e2e = None
     if not args.no_e2e:
-        Qh = Q.cpu().pin_memory()
-        Kh = K.cpu().pin_memory()
-        Vh = V.cpu().pin_memory()
-        Qd, Kd, Vd = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
-        idx_h = torch.empty(comp.keep_idx.shape, dtype=torch.int64).pin_memory()
-        kc_h = torch.empty(comp.k_out.shape, dtype=comp.k_out.dtype).pin_memory()
-        vc_h = torch.empty_like(kc_h).pin_memory()
-        h2d = Qh.numel() * Qh.element_size() + 2 * Kh.numel() * Kh.element_size()
-        d2h = idx_h.numel() * 8 + 2 * kc_h.numel() * kc_h.element_size()
-
-        del Qd, Kd, Vd
-        # ops.HostPipeline: every step copies its Q/K/V in and its outputs out; the
-        # host-to-device copy of step i + 1 overlaps the compression and the
-        # device-to-host copy of step i (two device slots, a stream per stage)
-        pipe = ops.HostPipeline(wl.B, wl.Hq, wl.Hkv, wl.Lq, wl.Lk, wl.D, wl.dtype, wl.window_size,
-                                wl.kernel_size, kl, device=dev)
-        ke = max(3, min(args.steps, 10))
-        items = [(Qh, Kh, Vh, idx_h, kc_h, vc_h)] * ke
-        pipe.run(items[:2]).synchronize()
+        h2d = d2h = 0
+        e2e_local = 0.0
+        if comp:
+            Qh = Q.cpu().pin_memory()
+            Kh = K.cpu().pin_memory()
+            Vh = V.cpu().pin_memory()
+            idx_h = torch.empty(comp.keep_idx.shape, dtype=torch.int64).pin_memory()
+            kc_h = torch.empty(comp.k_out.shape, dtype=comp.k_out.dtype).pin_memory()
+            vc_h = torch.empty_like(kc_h).pin_memory()
+            h2d = Qh.numel() * Qh.element_size() + 2 * Kh.numel() * Kh.element_size()
+            d2h = idx_h.numel() * 8 + 2 * kc_h.numel() * kc_h.element_size()
+            # ops.HostPipeline: every step copies its Q/K/V in and its outputs out; the
+            # host-to-device copy of step i + 1 overlaps the compression and the
+            # device-to-host copy of step i (two device slots, a stream per stage)
+            pipe = ops.HostPipeline(wl.B, nh * g, nh, wl.Lq, wl.Lk, wl.D, wl.dtype, wl.window_size,
+                                    wl.kernel_size, kl, device=dev)
+            ke = max(3, min(args.steps, 10))
+            items = [(Qh, Kh, Vh, idx_h, kc_h, vc_h)] * ke
+            pipe.run(items[:2]).synchronize()
         barrier()
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record(pipe.h2d)
-        pipe.run(items)
-        s1.record(pipe.d2h)
-        torch.cuda.synchronize(dev)
-        e2e_ms = max_over_ranks(s0.elapsed_time(s1) / ke)
-        e2e = {"value": n * positions / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+        if comp:
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(pipe.h2d)
+            pipe.run(items)
+            s1.record(pipe.d2h)
+            torch.cuda.synchronize(dev)
+            e2e_local = s0.elapsed_time(s1) / ke
+        rank_e2e = gather_ranks(e2e_local)
+        e2e_ms = max(rank_e2e)
+        h2d_all = gather_ranks(float(h2d))
+        e2e = {"value": positions / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(sum(h2d_all)),
+               "d2h_bytes_per_step": int(sum(gather_ranks(float(d2h)))), "ms_per_step": e2e_ms,
+               "rank_ms": rank_e2e,
+               "h2d_gbs_per_rank": [b / (t / 1e3) / 1e9 if t > 0 else 0.0 for b, t in zip(h2d_all, rank_e2e)],
+               "h2d_gbs_aggregate": sum(h2d_all) / (e2e_ms / 1e3) / 1e9,
                "path": "ops.HostPipeline over dropkv_compress (ctypes): pinned host Q/K/V -> HBM, "
                        "K_c/V_c/keep_idx -> pinned host, the copies of consecutive steps overlapped"}
-        del Qh, Kh, Vh, pipe
+        if comp:
+            del Qh, Kh, Vh, pipe
 
-    # ---- CPU baseline (rank 0, N=1) -----------------------------------------
-    cpu = None
+    # ---- config-5 ragged batch at this N (nested record) ----------------------
+    ragged = None
+    if not args.no_ragged:
+        del Qf, Kf, Vf
+        Q = K = V = None
+        torch.cuda.empty_cache()
+        ragged = ragged_record(args, rank, n, world, dev)
+
+    # ---- CPU baseline and the reference's GPU path (rank 0, N = 1) -------------
+    cpu = port = bar = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
-        rate, dt = cpu_oracle_rate(wl, wl.Hkv)
-        cores = blas_threads()
-        cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"oracle.compress (numpy fp32; BLAS {cores} threads) over the full layer "
-                         f"({wl.Hkv} KV heads x Lk={wl.Lk}), one run of {dt:.2f} s"}
+        r, why = reference_cpu_rate(wl, wl.Hkv)
+        if r is not None:
+            rate, dt, threads = r
+            cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "reference",
+                   "sample": f"reference DropKVCache(use_triton=False)._compute_keep_indices + _gather_compressed "
+                             f"(baseline/_ref, torch bf16 on CPU, {threads} threads, {cpu_model()}) over the "
+                             f"full layer ({wl.Hkv} KV heads x Lk={wl.Lk}), {dt:.2f} s after one warm-up run"}
+        prate, pdt = cpu_oracle_rate(wl, 1)
+        port = {"value": prate, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+                "sample": f"oracle.compress (numpy fp32) over 1 KV head x Lk={wl.Lk}, {pdt:.2f} s"}
+        if cpu is None:
+            cpu = dict(port, note=why)
+    if rank == 0 and n == 1 and not args.no_gpu_bar and comp:
+        bar, bar_idx = gpu_bar_child(args, dev)
+        if bar_idx is not None:
+            ours_idx = comp.keep_idx.cpu().numpy()
+            same = [len(set(bar_idx[0, h].tolist()) & set(ours_idx[0, h].tolist())) for h in range(wl.Hkv)]
+            bar["kept_set_agreement"] = float(sum(same)) / (wl.Hkv * kl)
+            bar["kept_set_differences_per_head"] = [kl - x for x in same]
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if n > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded, config-2 value distribution)", "config": config_of(wl, n),
             "hbm_frac": path_gbs / peak,
             "roofline": {"bound": "hbm", "achieved": score_gbs, "peak": peak, "unit": "GB/s",
                          "frac": score_gbs / peak, "traffic": traffic,
-                         "kernel": "scoring launches (dropkv_scores)",
+                         "kernel": f"scoring launches (dropkv_scores) over rank 0's {h1 - h0} KV heads",
                          "algorithmic_bytes": score_bytes, "ms": score_ms,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
             "path_roofline": {"bound": "hbm", "achieved": path_gbs, "peak": peak, "unit": "GB/s",
                               "frac": path_gbs / peak, "algorithmic_bytes": path_bytes,
-                              "ms": ms_per_step},
+                              "ms": ms_per_step, "per": "GPU (the layer's bytes over the ranks holding heads)"},
+            "rank_ms_per_step": rank_ms,
             "step_ms_min_max": [min(step_ms), max(step_ms)],
             "step": ("one dropkv_compress call (scorer, selection, gather) replayed from a CUDA graph"
                      if per_graph else "one dropkv_compress call"),
+            "checked": checked,
             "eager_ms_per_step": eager_ms,
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+            "cpu_baseline": cpu, "port_baseline": port, "gpu_bar": bar,
+            "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+            "ragged": ragged,
         }
         if phases is not None:
             line["scorer_phases_us"] = phases
@@ -447,112 +691,151 @@ def run_ours(args, rank, n, world):
 # ragged batch (config 5) across ranks
 # ---------------------------------------------------------------------------
 RAGGED_METRIC = "KV positions scored+compacted/sec, ragged batch (config 5)"
+RAGGED_RATIOS = (0.1, 0.25, 0.5)
+
+
+def ragged_plan(args, n):
+    from dropkv_b200.sharding import PARTITIONS, make_units, ragged_lengths
+    lengths = ragged_lengths(args.ragged_seqs, 4096, 65536, args.ragged_seed)
+    all_units = make_units(lengths, args.ragged_layers)
+    parts = PARTITIONS[args.ragged_partition](all_units, n)
+    return lengths, all_units, parts
+
+
+def ragged_inputs(args, units, dev):
+    """This rank's inputs: per sequence, its layers stacked along the batch axis
+    ([layers, Hkv, Lk, D]; a rank's layers of one sequence share Lk), the same
+    per-unit data whatever the partition. ``unit`` batching keeps one entry per
+    (sequence, layer) unit instead."""
+    import torch
+    from dropkv_b200.workloads import llama_layer, make_qkv
+    work = []
+    if args.ragged_batch == "unit":
+        for u in units:
+            wl = llama_layer(u.lk, seed=1000 * u.seq + u.layer + 7)
+            work.append((u.lk, make_qkv(wl, dev)))
+        return work
+    by_seq = {}
+    for u in units:
+        by_seq.setdefault(u.seq, []).append(u)
+    for seq in sorted(by_seq, key=lambda q: -by_seq[q][0].lk):
+        us = sorted(by_seq[seq], key=lambda u: u.layer)
+        wl0 = llama_layer(us[0].lk)
+        L = len(us)
+        Q = torch.empty(L, wl0.Hq, wl0.Lq, wl0.D, dtype=wl0.dtype, device=dev)
+        K = torch.empty(L, wl0.Hkv, wl0.Lk, wl0.D, dtype=wl0.dtype, device=dev)
+        V = torch.empty_like(K)
+        for i, u in enumerate(us):
+            q, k, v = make_qkv(llama_layer(u.lk, seed=1000 * u.seq + u.layer + 7), dev)
+            Q[i].copy_(q[0])
+            K[i].copy_(k[0])
+            V[i].copy_(v[0])
+            del q, k, v
+        work.append((wl0.Lk, (Q, K, V)))
+    return work
+
+
+def ragged_record(args, rank, n, world, dev, ratios=RAGGED_RATIOS, steps=5, warmup=2):
+    """Config 5 at this N: the ragged batch split across the ranks, one pass per
+    keep ratio timed as the max over ranks of CUDA-event device time (strong
+    scaling: the batch is fixed). Returns the record on rank 0, None elsewhere."""
+    import torch
+    import torch.distributed as dist
+    from dropkv_b200 import _lib, ops
+    from dropkv_b200.sharding import load_imbalance
+    from dropkv_b200.workloads import keep_len_rule, llama_layer
+
+    lengths, all_units, parts = ragged_plan(args, n)
+    work = ragged_inputs(args, parts[rank], dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def gather_ranks(x: float) -> list:
+        if not world:
+            return [x]
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        out = [torch.zeros_like(t) for _ in range(n)]
+        dist.all_gather(out, t)
+        return [float(o.item()) for o in out]
+
+    positions = sum(8 * u.lk for u in all_units)
+    peak, peak_kind = measured_peaks()
+    by_ratio, launches = {}, 0
+    for kr in ratios:
+        comps = []
+        for lk, (Q, K, V) in work:
+            comps.append((ops.Compressor(Q.shape[0], Q.shape[1], K.shape[1], Q.shape[2], lk, Q.shape[3], Q.dtype,
+                                         8, 11, keep_len_rule(lk, kr, 8), device=dev), (Q, K, V)))
+
+        def one_pass():
+            for comp, (Q, K, V) in comps:
+                comp.run(Q, K, V)
+
+        for _ in range(warmup):
+            one_pass()
+        if world:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        n0 = _lib.launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            one_pass()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        launches = _lib.launch_count() - n0
+        rank_ms = gather_ranks(e0.elapsed_time(e1) / steps)
+        del comps
+        torch.cuda.empty_cache()
+        ms = max(rank_ms)
+        path_bytes = sum(llama_layer(u.lk, keep_ratio=kr).algorithmic_bytes() for u in all_units)
+        gbs = path_bytes / (ms / 1e3) / 1e9 / n
+        by_ratio[str(kr)] = {
+            "value": positions / (ms / 1e3), "ms_per_pass": ms, "rank_ms": rank_ms,
+            "measured_imbalance": ms / (sum(rank_ms) / len(rank_ms)),
+            "hbm_frac_per_gpu": gbs / peak, "gpu_launches_per_pass_rank0": launches // steps}
+    del work
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    return {
+        "metric": RAGGED_METRIC, "unit": UNIT, "n_gpus": n, "scaling": "strong", "steps": steps,
+        "warmup": warmup, "by_keep_ratio": by_ratio,
+        "config": {"workload": f"ragged_b{args.ragged_seqs}_lk4096-65536_{args.ragged_layers}layers",
+                   "sequences_lk": lengths, "layers": args.ragged_layers, "Hq": 32, "Hkv": 8, "D": 128,
+                   "Lq": 8, "window": 8, "kernel_size": 11, "units": len(all_units),
+                   "units_per_rank": [len(p) for p in parts], "planned_imbalance": load_imbalance(parts),
+                   "partition": args.ragged_partition, "batching": args.ragged_batch,
+                   "calls_per_pass_rank0": len(ragged_plan(args, n)[2][0]) if args.ragged_batch == "unit"
+                   else len({u.seq for u in parts[0]}),
+                   "parallelism": f"{n} ranks, (sequence, layer) units, {args.ragged_partition} partition, "
+                                  "no collective",
+                   "timing": "CUDA events per rank after a barrier, max over ranks",
+                   "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+    }
 
 
 def run_ragged(args, rank, n, world):
     import torch
-    import torch.distributed as dist
-    from dropkv_b200 import _lib, ops
-    from dropkv_b200.sharding import PARTITIONS, load_imbalance, make_units, ragged_lengths
-    from dropkv_b200.workloads import llama_layer, make_qkv
-
     dev = torch.device("cuda", torch.cuda.current_device())
-    lengths = ragged_lengths(args.ragged_seqs, 4096, 65536, args.ragged_seed)
-    all_units = make_units(lengths, args.ragged_layers)
-    parts = PARTITIONS[args.ragged_partition](all_units, n)
-    mine = parts[rank]
-    comps, work = {}, []
-    if args.ragged_batch == "unit":
-        for u in mine:
-            wl = llama_layer(u.lk, keep_ratio=args.keep_ratio, seed=1000 * u.seq + u.layer + 7)
-            if u.lk not in comps:
-                comps[u.lk] = ops.Compressor(wl.B, wl.Hq, wl.Hkv, wl.Lq, wl.Lk, wl.D, wl.dtype,
-                                             wl.window_size, wl.kernel_size, wl.keep_len(), device=dev)
-            work.append((comps[u.lk], make_qkv(wl, dev)))
-    else:
-        # the rank's layers of one sequence share Lk: one call over all their
-        # (layer, KV head) rows, the layers stacked along the batch axis
-        by_seq = {}
-        for u in mine:
-            by_seq.setdefault(u.seq, []).append(u)
-        for seq in sorted(by_seq, key=lambda q: -by_seq[q][0].lk):
-            units = sorted(by_seq[seq], key=lambda u: u.layer)
-            wl0 = llama_layer(units[0].lk, keep_ratio=args.keep_ratio)
-            L = len(units)
-            Q = torch.empty(L, wl0.Hq, wl0.Lq, wl0.D, dtype=wl0.dtype, device=dev)
-            K = torch.empty(L, wl0.Hkv, wl0.Lk, wl0.D, dtype=wl0.dtype, device=dev)
-            V = torch.empty_like(K)
-            for i, u in enumerate(units):  # the same per-unit data as the unit mode
-                q, k, v = make_qkv(llama_layer(u.lk, keep_ratio=args.keep_ratio,
-                                               seed=1000 * u.seq + u.layer + 7), dev)
-                Q[i].copy_(q[0])
-                K[i].copy_(k[0])
-                V[i].copy_(v[0])
-                del q, k, v
-            comp = ops.Compressor(L, wl0.Hq, wl0.Hkv, wl0.Lq, wl0.Lk, wl0.D, wl0.dtype, wl0.window_size,
-                                  wl0.kernel_size, wl0.keep_len(), device=dev)
-            work.append((comp, (Q, K, V)))
-    stream = torch.cuda.current_stream(dev)
-
-    def one_pass():
-        for comp, (Q, K, V) in work:
-            comp.run(Q, K, V)
-
-    def barrier():
-        if world:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    for _ in range(args.warmup):
-        one_pass()
-    barrier()
     clocks = ClockSampler(gpu_uuid(dev))
     clocks.start()
-    time.sleep(0.3)
-    n_launch0 = _lib.launch_count()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        one_pass()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    launches = _lib.launch_count() - n_launch0
+    rec = ragged_record(args, rank, n, world, dev, ratios=(args.keep_ratio,), steps=args.steps,
+                        warmup=args.warmup)
     clk = clocks.stop()
-    total_ms = e0.elapsed_time(e1)
-    if world:
-        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
     if rank != 0:
         return
-    ms_per_step = total_ms / args.steps
-    hkv = 8
-    positions = sum(hkv * u.lk for u in all_units)
-    value = positions * args.steps / (total_ms / 1e3)
-    path_bytes = sum(llama_layer(u.lk, keep_ratio=args.keep_ratio).algorithmic_bytes() for u in all_units)
-    peak, peak_kind = measured_peaks()
-    per_gpu_gbs = path_bytes / (ms_per_step / 1e3) / 1e9 / n
+    r = rec["by_keep_ratio"][str(args.keep_ratio)]
     line = {
-        "metric": RAGGED_METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "metric": RAGGED_METRIC, "value": r["value"], "unit": UNIT, "n_gpus": n, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_pass"], "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, config-2 value distribution per unit)",
-        "config": {"workload": f"ragged_b{args.ragged_seqs}_lk4096-65536_{args.ragged_layers}layers",
-                   "sequences_lk": lengths, "layers": args.ragged_layers, "Hq": 32, "Hkv": hkv, "D": 128,
-                   "Lq": 8, "window": 8, "kernel_size": 11, "keep_ratio": args.keep_ratio,
-                   "units": len(all_units), "units_per_rank": [len(p) for p in parts],
-                   "calls_per_pass_rank0": len(work), "batching": args.ragged_batch,
-                   "load_imbalance": load_imbalance(parts),
-                   "partition": args.ragged_partition,
-                   "parallelism": f"{n} ranks, (sequence, layer) units, {args.ragged_partition} partition, "
-                                  "no collective",
-                   "l2": "distinct inputs per unit, whole batch far above the 126 MB L2"},
-        "roofline": {"bound": "hbm", "achieved": per_gpu_gbs, "peak": peak, "unit": "GB/s",
-                     "frac": per_gpu_gbs / peak, "traffic": None,
-                     "kernel": "whole path (scores + select + gather), per GPU",
-                     "algorithmic_bytes": path_bytes, "ms": ms_per_step,
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
-        "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clk,
+        "config": dict(rec["config"], keep_ratio=args.keep_ratio,
+                       l2="distinct inputs per unit, whole batch far above the 126 MB L2"),
+        "rank_ms": r["rank_ms"], "measured_imbalance": r["measured_imbalance"],
+        "hbm_frac_per_gpu": r["hbm_frac_per_gpu"],
+        "cpu_baseline": None, "e2e": None, "gpu_launches": r["gpu_launches_per_pass_rank0"] * args.steps,
+        "clocks": clk,
     }
     print(json.dumps(line), flush=True)
 
@@ -915,6 +1198,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1")) > 1
     rank = int(os.environ.get("RANK", "0"))
     n = int(os.environ.get("WORLD_SIZE", str(args.gpus))) if world else 1
+    if args.gpu_bar_only:
+        run_gpu_bar(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, n)
         return

@@ -17,7 +17,7 @@ Public API (the reference's names and semantics):
 """
 
 from ._lib import DropKVError, version
-from .cache import Cache, DropKVCache, DynamicCache, prefill_chunked
+from .cache import DropKVCache, prefill_chunked
 from .ops import (Compressor, HostPipeline, compress, decode_attention, dropkv_scores_cuda,
                   gather_compressed, scores, select_keep_indices)
 
@@ -25,7 +25,7 @@ from .ops import (Compressor, HostPipeline, compress, decode_attention, dropkv_s
 dropkv_scores_triton = dropkv_scores_cuda
 
 __all__ = [
-    "Cache", "DynamicCache", "DropKVCache", "prefill_chunked", "DropKVError", "version",
+    "DropKVCache", "prefill_chunked", "DropKVError", "version",
     "compress", "decode_attention", "dropkv_scores_cuda", "dropkv_scores_triton", "gather_compressed",
     "scores", "select_keep_indices", "Compressor", "HostPipeline",
 ]

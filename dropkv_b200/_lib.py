@@ -31,8 +31,10 @@ SIGNATURES = {
     "dropkv_scores_static": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_int,
                                       _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int,
                                       _c_p, _c_p]),
+    "dropkv_scores_static_status": (_c_int, [_c_int] * 7 + [_c_p, _c_p]),
     "dropkv_scorer_for": (_c_int, [_c_int] * 7),
     "dropkv_set_scorer": (_c_int, [_c_int]),
+    "dropkv_test_scorer_waits": (_c_int, [ctypes.c_uint64, _c_int]),
     "dropkv_scores_status_offset": (_c_sz, [_c_int] * 7),
     "dropkv_selftest_tcgen05": (_c_int, [_c_int, _c_p, _c_p, _c_int, _c_p, _c_p, _c_p]),
     "dropkv_select_workspace_size": (_c_sz, [_c_int] * 3),

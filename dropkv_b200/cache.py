@@ -18,7 +18,6 @@ positions (dropkv_cache.py:466-467).
 from __future__ import annotations
 
 import logging
-from collections.abc import Iterable
 from typing import Any, Optional
 
 import torch
@@ -27,147 +26,53 @@ from . import _lib, ops
 
 logger = logging.getLogger(__name__)
 
-__all__ = ["Cache", "DynamicCache", "DropKVCache", "prefill_chunked"]
+__all__ = ["DropKVCache", "prefill_chunked"]
 
 
-class Cache:
-    """Minimal cache base (the interface of dropkv_cache.py:13-101)."""
+class _KVStore:
+    """Per-layer K/V storage under DropKVCache's state machine.
 
-    is_compileable = False
+    ``key_cache[i]`` / ``value_cache[i]`` hold layer i's retained K and V
+    ([B, Hkv, L_i, D]); ``_seen_tokens`` counts the tokens layer 0 has received
+    (the logical sequence length that positions continue from after an eviction).
+    Layers are indexed by ``cache[i]`` -> (K, V), iterated in order and counted by
+    ``len``.  Only what DropKVCache and its callers use is here: no beam-search or
+    legacy-format conversions.
+    """
 
-    def update(self, query_states, key_states, value_states, layer_idx, cache_kwargs=None):
-        raise NotImplementedError("Make sure to implement `update` in a subclass.")
-
-    def get_seq_length(self, layer_idx: Optional[int] = 0) -> int:
-        raise NotImplementedError("Make sure to implement `get_seq_length` in a subclass.")
-
-    def get_max_cache_shape(self) -> Optional[int]:
-        raise NotImplementedError("Make sure to implement `get_max_cache_shape` in a subclass.")
-
-    def get_usable_length(self, new_seq_length: int, layer_idx: Optional[int] = 0) -> int:
-        max_length = self.get_max_cache_shape()
-        previous = self.get_seq_length(layer_idx)
-        if max_length is not None and previous + new_seq_length > max_length:
-            return max_length - new_seq_length
-        return previous
-
-    def reorder_cache(self, beam_idx: torch.LongTensor):
-        for i in range(len(self.key_cache)):
-            if self.key_cache[i].numel():
-                self.key_cache[i] = self.key_cache[i].index_select(0, beam_idx.to(self.key_cache[i].device))
-            if self.value_cache[i].numel():
-                self.value_cache[i] = self.value_cache[i].index_select(0, beam_idx.to(self.value_cache[i].device))
-
-    @property
-    def seen_tokens(self):
-        return getattr(self, "_seen_tokens", None)
-
-    def get_mask_sizes(self, cache_position: torch.Tensor, layer_idx: int) -> tuple[int, int]:
-        return cache_position.shape[0] + self.get_seq_length(), 0
-
-
-class DynamicCache(Cache):
-    """List-of-tensors KV store, one [B, Hkv, L, D] pair per layer (dropkv_cache.py:104-307)."""
-
-    def __init__(self, _distributed_cache_data: Optional[Iterable] = None) -> None:
-        super().__init__()
+    def __init__(self) -> None:
         self._seen_tokens = 0
         self.key_cache: list[torch.Tensor] = []
         self.value_cache: list[torch.Tensor] = []
-        if _distributed_cache_data is not None:
-            for k, v in _distributed_cache_data:
-                self.key_cache.append(k)
-                self.value_cache.append(v)
 
-    def __getitem__(self, layer_idx: int):
-        if layer_idx < len(self):
-            return self.key_cache[layer_idx], self.value_cache[layer_idx]
-        raise KeyError(f"Cache only has {len(self)} layers, attempted to access layer with index {layer_idx}")
-
-    def __iter__(self):
-        for i in range(len(self)):
-            yield self.key_cache[i], self.value_cache[i]
-
-    def __len__(self):
+    def __len__(self) -> int:
         return len(self.key_cache)
 
-    def update(self, query_states, key_states, value_states, layer_idx, cache_kwargs=None):
-        if layer_idx == 0:
-            self._seen_tokens += key_states.shape[-2]
-        if key_states is not None:
-            if len(self.key_cache) <= layer_idx:
-                while len(self.key_cache) < layer_idx:
-                    self.key_cache.append(torch.tensor([]))
-                    self.value_cache.append(torch.tensor([]))
-                self.key_cache.append(key_states)
-                self.value_cache.append(value_states)
-            elif not self.key_cache[layer_idx].numel():
-                self.key_cache[layer_idx] = key_states
-                self.value_cache[layer_idx] = value_states
-            else:
-                self.key_cache[layer_idx] = torch.cat([self.key_cache[layer_idx], key_states], dim=-2)
-                self.value_cache[layer_idx] = torch.cat([self.value_cache[layer_idx], value_states], dim=-2)
+    def __getitem__(self, layer_idx: int):
+        if not 0 <= layer_idx < len(self.key_cache):
+            raise KeyError(f"layer {layer_idx} is not in this cache ({len(self.key_cache)} layers)")
         return self.key_cache[layer_idx], self.value_cache[layer_idx]
 
+    def __iter__(self):
+        return iter(list(zip(self.key_cache, self.value_cache)))
+
     def get_seq_length(self, layer_idx: Optional[int] = 0) -> int:
-        if len(self.key_cache) <= layer_idx or not self.key_cache[layer_idx].numel():
-            return 0
-        return self.key_cache[layer_idx].shape[-2]
+        raise NotImplementedError
 
-    def get_max_cache_shape(self) -> Optional[int]:
-        return None
-
-    def to_legacy_cache(self):
-        return tuple((self.key_cache[i], self.value_cache[i]) for i in range(len(self)))
-
-    @classmethod
-    def from_legacy_cache(cls, past_key_values=None):
-        cache = cls()
-        if past_key_values is not None:
-            for i, (k, v) in enumerate(past_key_values):
-                cache.update(None, k, v, i)
-        return cache
-
-    def crop(self, max_length: int):
+    def crop(self, max_length: int) -> None:
+        """Truncate every layer to its first ``max_length`` positions (a negative
+        value drops that many from the end) when the cache's length exceeds it;
+        the length is ``get_seq_length()``, as in the reference's base cache
+        (dropkv_cache.py:255-269), so for DropKVCache it is the tokens seen."""
         if max_length < 0:
             max_length = self.get_seq_length() - abs(max_length)
         if self.get_seq_length() <= max_length:
             return
         self._seen_tokens = max_length
-        for i in range(len(self.key_cache)):
-            if self.key_cache[i].numel():
-                self.key_cache[i] = self.key_cache[i][..., :max_length, :]
+        for i, k in enumerate(self.key_cache):
+            if k.numel():
+                self.key_cache[i] = k[..., :max_length, :]
                 self.value_cache[i] = self.value_cache[i][..., :max_length, :]
-
-    def batch_split(self, full_batch_size: int, split_size: int):
-        out = []
-        for i in range(0, full_batch_size, split_size):
-            c = DynamicCache()
-            c._seen_tokens = self._seen_tokens
-            c.key_cache = [t[i:i + split_size] for t in self.key_cache]
-            c.value_cache = [t[i:i + split_size] for t in self.value_cache]
-            out.append(c)
-        return out
-
-    @classmethod
-    def from_batch_splits(cls, splits, **kwargs):
-        cache = cls(**kwargs)
-        for i in range(len(splits[0])):
-            ks = [s.key_cache[i] for s in splits if s.key_cache[i].numel()]
-            vs = [s.value_cache[i] for s in splits if s.value_cache[i].numel()]
-            if ks:
-                cache.update(None, torch.cat(ks, dim=0), torch.cat(vs, dim=0), i)
-        return cache
-
-    def batch_repeat_interleave(self, repeats: int):
-        for i in range(len(self)):
-            self.key_cache[i] = self.key_cache[i].repeat_interleave(repeats, dim=0)
-            self.value_cache[i] = self.value_cache[i].repeat_interleave(repeats, dim=0)
-
-    def batch_select_indices(self, indices: torch.Tensor):
-        for i in range(len(self)):
-            self.key_cache[i] = self.key_cache[i][indices, ...]
-            self.value_cache[i] = self.value_cache[i][indices, ...]
 
 
 _VALID_MODES = ("single_pass", "accumulate", "evict_accumulated")
@@ -269,7 +174,7 @@ class _LayerRows:
         self.n = keep_len
 
 
-class DropKVCache(DynamicCache):
+class DropKVCache(_KVStore):
     """KV cache that evicts at prefill with the DropKV score (CUDA backend)."""
 
     def __init__(self, keep_ratio: float = 0.1, window_size: int = 8, kernel_size: int = 11,
@@ -301,7 +206,7 @@ class DropKVCache(DynamicCache):
 
     def _rebuild_rows(self):
         """Row buffers again from key_cache / value_cache after they were replaced
-        by a whole-cache operation (crop, batch reordering)."""
+        by a whole-cache operation (crop)."""
         if self.storage != "buffer":
             return
         self._rows = []
@@ -313,14 +218,6 @@ class DropKVCache(DynamicCache):
 
     def crop(self, max_length: int):
         super().crop(max_length)
-        self._rebuild_rows()
-
-    def batch_repeat_interleave(self, repeats: int):
-        super().batch_repeat_interleave(repeats)
-        self._rebuild_rows()
-
-    def batch_select_indices(self, indices: torch.Tensor):
-        super().batch_select_indices(indices)
         self._rebuild_rows()
 
     def batch_split(self, full_batch_size: int, split_size: int):

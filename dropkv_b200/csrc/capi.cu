@@ -41,13 +41,16 @@ int check_launch(const char* what, int launches) {
 }
 
 int num_sms_current_device() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];  // zero: not queried yet
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (dev < 64 && cache[dev] > 0) return cache[dev];
+  if (dev >= 0 && dev < 64) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-  if (dev < 64) cache[dev] = n;
+  if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
@@ -165,10 +168,14 @@ static int check_select_args(int B, int Hkv, int Lk, int kernel_size, int protec
 // needs no allocation.  Its address is looked up once per device (with that device
 // current) and cached.
 static __device__ __align__(256) unsigned char g_static_scratch[DROPKV_STATIC_SCRATCH_BYTES];
+// A zero status word: what dropkv_scores_static_status copies for problems the
+// CUDA-core scorer serves (it has no bounded waits, so no status of its own).
+static __device__ __align__(16) int g_zero_status = 0;
 static std::mutex g_static_mu;
 static void* g_static_addr[64] = {nullptr};
+static void* g_zero_addr[64] = {nullptr};
 
-static int static_scratch_address(void** out) {
+static int static_scratch_address(void** out, void** zero_word = nullptr) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
@@ -176,13 +183,20 @@ static int static_scratch_address(void** out) {
   std::lock_guard<std::mutex> lock(g_static_mu);
   if (!g_static_addr[dev]) {
     void* p = nullptr;
+    void* z = nullptr;
     e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess || !p)
       return fail(DROPKV_ERR_CUDA, "cudaGetSymbolAddress of the static scratch on device %d: %s", dev,
                   cudaGetErrorString(e));
+    e = cudaGetSymbolAddress(&z, g_zero_status);
+    if (e != cudaSuccess || !z)
+      return fail(DROPKV_ERR_CUDA, "cudaGetSymbolAddress of the zero status word on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    g_zero_addr[dev] = z;
     g_static_addr[dev] = p;
   }
   *out = g_static_addr[dev];
+  if (zero_word) *zero_word = g_zero_addr[dev];
   return DROPKV_OK;
 }
 
@@ -211,6 +225,12 @@ size_t dropkv_scores_status_offset(int dtype, int B, int Hq, int Hkv, int Lk, in
   const int M = (Hq / Hkv) * window;
   if (!use_tc(dtype, B, Hkv, Lk, M, D)) return (size_t)-1;
   return tc_status_offset(M, D, B * Hkv, Lk);
+}
+
+int dropkv_test_scorer_waits(uint64_t wait_limit_ns, int block_group_barrier) {
+  tc_test_set_wait_ns(wait_limit_ns);
+  tc_test_block_barrier(block_group_barrier);
+  return DROPKV_OK;
 }
 
 int dropkv_set_scorer(int mode) {
@@ -255,6 +275,26 @@ int dropkv_scores_static(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss
   ScoreProblem p = make_problem(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, B, Hq, Hkv, Lk, D, window, eps,
                                 round_p, scores);
   return run_scores(p, dtype, ws, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dropkv_scores_static_status(int dtype, int B, int Hq, int Hkv, int Lk, int D, int window, int* status_out,
+                                void* stream) {
+  if (!status_out) return fail(DROPKV_ERR_ARG, "status_out must be non-NULL");
+  if (!elem_bytes_of(dtype)) return fail(DROPKV_ERR_ARG, "unknown dtype %d", dtype);
+  if (B < 1 || Hq < 1 || Hkv < 1 || Lk < 1 || D < 1 || window < 1 || Hq % Hkv)
+    return fail(DROPKV_ERR_ARG, "invalid problem sizes");
+  void* base = nullptr;
+  void* zero = nullptr;
+  int rc = static_scratch_address(&base, &zero);
+  if (rc) return rc;
+  const int M = (Hq / Hkv) * window;
+  const void* src = use_tc(dtype, B, Hkv, Lk, M, D)
+                        ? static_cast<const void*>(reinterpret_cast<char*>(base) + tc_status_offset(M, D, B * Hkv, Lk))
+                        : static_cast<const void*>(zero);
+  cudaError_t e = cudaMemcpyAsync(status_out, src, sizeof(int), cudaMemcpyDefault,
+                                  reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "copy of the static status word: %s", cudaGetErrorString(e));
+  return DROPKV_OK;
 }
 
 size_t dropkv_select_workspace_size(int B, int Hkv, int Lk) {

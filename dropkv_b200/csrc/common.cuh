@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -97,6 +98,18 @@ ScorePlan plan_scores(int B, int Hkv, int Lk, int M, int D);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// One bit per device (index < 64) recording that a per-device set-up step (kernel
+// attributes) has run.  Several host threads may call into the library at once:
+// the bits are read and set atomically, and a set-up step that two threads race
+// on runs twice, which is harmless because each step is idempotent.
+struct DeviceOnce {
+  std::atomic<unsigned long long> bits{0};
+  bool done(int dev) const { return dev >= 0 && dev < 64 && ((bits.load(std::memory_order_acquire) >> dev) & 1ull); }
+  void mark(int dev) {
+    if (dev >= 0 && dev < 64) bits.fetch_or(1ull << dev, std::memory_order_release);
+  }
+};
+
 // Launchers implemented per translation unit.
 int launch_scores_simt(const ScoreProblem& p, const ScorePlan& plan, void* ws, cudaStream_t st,
                        int dtype);
@@ -104,6 +117,8 @@ bool tc_supported(int dtype, int M, int D, int BH, int Lk);
 size_t tc_workspace_bytes(int M, int D, int BH, int Lk);
 size_t tc_status_offset(int M, int D, int BH, int Lk);
 int launch_scores_tc(const ScoreProblem& p, int dtype, void* ws, cudaStream_t st);
+void tc_test_set_wait_ns(uint64_t ns);
+void tc_test_block_barrier(int on);
 
 struct SelectPlan {
   size_t off_keys;   // uint32 [BH, Lk]

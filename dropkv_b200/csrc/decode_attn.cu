@@ -357,10 +357,13 @@ int da_keys_per_stage(int mr) { return mr <= 4 ? DaCfg<4>::KC : DaCfg<8>::KC; }
 // Clusters of `cl` CTAs that can be resident at once (a cluster must fit in one
 // GPC, and GPCs differ in size), cached per device, kernel variant and size.
 int da_active_clusters(DaKernel kern, int var, int cl, int threads, int smem) {
-  static int cache[16][DA_MAXCL + 1][16];
+  static std::atomic<int> cache[16][DA_MAXCL + 1][16];  // zero: not queried yet
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 16 && cache[var][cl][dev] > 0) return cache[var][cl][dev];
+  if (dev >= 0 && dev < 16) {
+    const int c = cache[var][cl][dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cl);
   cfg.blockDim = dim3(threads);
@@ -377,7 +380,7 @@ int da_active_clusters(DaKernel kern, int var, int cl, int threads, int smem) {
     cudaGetLastError();
     return 1 << 20;
   }
-  if (dev < 16) cache[var][cl][dev] = n;
+  if (dev >= 0 && dev < 16) cache[var][cl][dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
@@ -418,12 +421,12 @@ int launch_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q
     var = D == 128 ? 8 : 12;
   }
   var += mr == 1 ? 0 : (mr == 2 ? 1 : (mr == 4 ? 2 : 3));
-  static unsigned long long done[16] = {};  // attributes set, per variant and device
-  if (dev >= 64 || !(done[var] & (1ull << dev))) {
+  static DeviceOnce done[16];  // attributes set, per variant and device
+  if (!done[var].done(dev)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
         cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       return fail(DROPKV_ERR_CUDA, "cannot set decode attention kernel attributes");
-    if (dev < 64) done[var] |= (1ull << dev);
+    done[var].mark(dev);
   }
   // CTAs per cluster: the size that finishes soonest, counting the waves the
   // launch's clusters need and the key stages each CTA streams; at most 16

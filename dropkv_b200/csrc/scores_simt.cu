@@ -358,13 +358,15 @@ size_t score_smem() {
 template <typename T, int D>
 int launch_typed(const ScoreProblem& p, const ScorePlan& plan, float* ws, cudaStream_t st) {
   size_t fs = fwd_smem<T, D>(), ss = score_smem<T, D>();
-  static unsigned long long attr_done = 0;  // one bit per device
+  static DeviceOnce attr_done;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(attr_done & (1ull << dev))) {
-    cudaFuncSetAttribute(fwd_partial_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fs);
-    cudaFuncSetAttribute(score_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss);
-    if (dev < 64) attr_done |= (1ull << dev);
+  if (!attr_done.done(dev)) {
+    if (cudaFuncSetAttribute(fwd_partial_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fs) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(score_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss) != cudaSuccess)
+      return fail(DROPKV_ERR_CUDA, "cannot set shared memory sizes of the CUDA-core scorer");
+    attr_done.mark(dev);
   }
   dim3 g1(plan.splits, plan.BH);
   fwd_partial_kernel<T, D><<<g1, NT, fs, st>>>(p, plan, ws);

@@ -35,6 +35,7 @@
 // the launch); every wait in the kernel gives up after a timeout, records a
 // device status and lets the CTA run to its end without further waits, so a
 // fault in this logic ends the kernel instead of hanging the GPU.
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <type_traits>
@@ -51,14 +52,15 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
+  // looked up once per process (a function-local static: initialised by one thread)
+  static const EncodeTiledFn fn = []() -> EncodeTiledFn {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
+      return reinterpret_cast<EncodeTiledFn>(p);
+    return nullptr;
+  }();
   return fn;
 }
 
@@ -108,7 +110,10 @@ constexpr int NEPI = 512;                    // epilogue threads (warps 0-15)
 constexpr int NEW = NEPI / 32;               // epilogue warps
 constexpr int NTH = NEPI + 64;               // + TMA producer warp + MMA warp
 constexpr int WARP_TMA = NEW, WARP_MMA = NEW + 1;
-constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
+// Waits for the hardware's own completions (in-flight TMA copies, committed MMAs)
+// give up after 1 s; waits on other roles and on other CTAs use TcArgs::wait_ns
+// (1 s unless a test shortens it).
+constexpr uint64_t kWaitNs = 1000000000ull;
 constexpr int kMaxGs = 256;                  // CTAs per head group (at most)
 constexpr int kWts = 1024;                   // merge maxima / sums buffers (floats each)
 constexpr int kMaxTiles = 30;                // TMEM logit tiles per CTA and head (N = 16)
@@ -138,6 +143,7 @@ struct TcArgs {
   int* status;   // device status word (0 = ok)
   int q_tma;     // 1: the TMA warp loads the Q window (qmap), 0: the epilogue stages it
   unsigned long long* trace;  // per CTA and round: globaltimer at phase ends
+  uint64_t wait_ns;  // limit of a wait on another role or CTA, then status + abort
 };
 
 // Phase timestamps recorded by epilogue thread 0 of every CTA (ns, globaltimer):
@@ -464,7 +470,7 @@ __global__ void __launch_bounds__(NTH, 1)
     const uint64_t t_start = tc::globaltimer_ns();
     while (!tc::mbar_try_wait(b, parity)) {
       if (*vabort) return false;
-      if (tc::globaltimer_ns() - t_start > kWaitNs) {
+      if (tc::globaltimer_ns() - t_start > a.wait_ns) {
         fail_wait(code);
         return false;
       }
@@ -832,7 +838,7 @@ __global__ void __launch_bounds__(NTH, 1)
             asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
             if (v >= a.gs) break;
             if (*vabort) break;
-            if (tc::globaltimer_ns() - t_start > kWaitNs) { fail_wait(35); break; }
+            if (tc::globaltimer_ns() - t_start > a.wait_ns) { fail_wait(35); break; }
           }
           __threadfence();
         }
@@ -1100,6 +1106,16 @@ __global__ void __launch_bounds__(NTH, 1)
 // ---------------------------------------------------------------------------
 // Host planning and launch
 // ---------------------------------------------------------------------------
+// Test hooks (process-wide): the limit of the scorer's waits on other roles and
+// CTAs, and a switch that makes the first group barrier of every launch
+// unreachable, so that a test can drive the timeout path on a GPU without any
+// fault: the waits give up, the kernel records a status and ends.
+static std::atomic<uint64_t> g_wait_ns{kWaitNs};
+static std::atomic<int> g_block_barrier{0};
+
+void tc_test_set_wait_ns(uint64_t ns) { g_wait_ns.store(ns ? ns : kWaitNs); }
+void tc_test_block_barrier(int on) { g_block_barrier.store(on ? 1 : 0); }
+
 struct TcPlan {
   bool ok;
   int npad, tmax, tiles, gs, groups, rounds, nctas;
@@ -1180,16 +1196,21 @@ static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cuda
   a.part_y = reinterpret_cast<float*>(base + t.off_py);
   a.y_g = reinterpret_cast<float*>(base + t.off_y);
   a.lse_g = reinterpret_cast<float*>(base + t.off_lse);
+  a.wait_ns = g_wait_ns.load();
   if (cudaMemsetAsync(base + t.off_ctr, 0, t.off_pm - t.off_ctr, st) != cudaSuccess)
     return fail(DROPKV_ERR_CUDA, "memset of barrier counters failed");
+  // test hook: head 0's first group-barrier counter starts negative (0x80808080),
+  // so the arrivals of its CTAs never reach the group size
+  if (g_block_barrier.load() && cudaMemsetAsync(base + t.off_ctr, 0x80, 4, st) != cudaSuccess)
+    return fail(DROPKV_ERR_CUDA, "memset of the blocked barrier counter failed");
   auto kern = fused_scores_kernel<T, D, NPAD, NS, NPB, ROUND>;
-  static unsigned long long attr_done = 0;
+  static DeviceOnce attr_done;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64 || !(attr_done & (1ull << dev))) {
+  if (!attr_done.done(dev)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC) != cudaSuccess)
       return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %d", L::ALLOC);
-    if (dev < 64) attr_done |= (1ull << dev);
+    attr_done.mark(dev);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(t.nctas);

@@ -448,17 +448,17 @@ static SgKernel sg_kernel(bool r5, int kpt, int* variant) {
 // Function attributes, set once per device and variant: the largest dynamic
 // shared memory any chunk can ask for, and 16-CTA clusters.
 static int sg_prepare(SgKernel kern, int variant, size_t smem) {
-  static unsigned long long done[SG_VARIANTS] = {};
+  static DeviceOnce done[SG_VARIANTS];
   const int max_dyn = 227 * 1024 - (int)sizeof(SgShared);
   if (smem > (size_t)max_dyn) return fail(DROPKV_ERR_UNSUPPORTED, "cluster select needs %zu bytes", smem);
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && (done[variant] & (1ull << dev))) return DROPKV_OK;
+  if (done[variant].done(dev)) return DROPKV_OK;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn) != cudaSuccess)
     return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %d for the cluster select", max_dyn);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
     return fail(DROPKV_ERR_CUDA, "cannot allow 16-CTA clusters for the cluster select");
-  if (dev < 64) done[variant] |= (1ull << dev);
+  done[variant].mark(dev);
   return DROPKV_OK;
 }
 
@@ -468,14 +468,17 @@ static int sg_prepare(SgKernel kern, int variant, size_t smem) {
 // upper end, so the answer is never too high).
 static int sg_active_clusters(SgKernel kern, int variant, int cl, size_t smem) {
   constexpr int kDevs = 16, kSteps = 29;  // 29 steps of 8 KB cover 227 KB
-  static int cache[SG_VARIANTS][5][kDevs][kSteps];
+  static std::atomic<int> cache[SG_VARIANTS][5][kDevs][kSteps];  // zero: not queried yet
   int dev = 0;
   cudaGetDevice(&dev);
   int lg = 0;
   while ((1 << lg) < cl) ++lg;
   const int step = (int)std::min<size_t>(kSteps - 1, smem / 8192);
   const size_t smem_q = std::min<size_t>((size_t)(step + 1) * 8192, 227 * 1024 - sizeof(SgShared));  // <= max_dyn
-  if (dev < kDevs && cache[variant][lg][dev][step] > 0) return cache[variant][lg][dev][step];
+  if (dev >= 0 && dev < kDevs) {
+    const int c = cache[variant][lg][dev][step].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cl);
   cfg.blockDim = dim3(SG_NT);
@@ -492,7 +495,7 @@ static int sg_active_clusters(SgKernel kern, int variant, int cl, size_t smem) {
     cudaGetLastError();  // clear the query's error; assume every cluster is resident
     return 1 << 20;
   }
-  if (dev < kDevs) cache[variant][lg][dev][step] = n;
+  if (dev >= 0 && dev < kDevs) cache[variant][lg][dev][step].store(n, std::memory_order_relaxed);
   return n;
 }
 

@@ -87,6 +87,15 @@ def rank_plan(rank: int, n_ranks: int, lengths: list[int], layers: int, method: 
     return PARTITIONS[method](make_units(lengths, layers), n_ranks)[rank]
 
 
+def head_range(rank: int, n_ranks: int, n_heads: int) -> tuple[int, int]:
+    """KV heads [h0, h1) of one layer that rank ``rank`` of ``n_ranks`` scores when a
+    single layer is split by KV head (contiguous runs, sizes differing by at most
+    one; ranks beyond the head count get an empty range)."""
+    if not 0 <= rank < n_ranks:
+        raise ValueError(f"rank {rank} outside [0, {n_ranks})")
+    return (rank * n_heads) // n_ranks, ((rank + 1) * n_heads) // n_ranks
+
+
 def load_imbalance(parts: list[list[Unit]]) -> float:
     """Largest rank load over the mean load (1.0 = perfect balance)."""
     loads = [sum(u.lk for u in p) for p in parts]

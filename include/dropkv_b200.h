@@ -92,6 +92,17 @@ DROPKV_API int dropkv_scorer_for(int dtype, int B, int Hq, int Hkv, int Lk, int 
  * fail with DROPKV_ERR_UNSUPPORTED).  For testing one path against the other. */
 DROPKV_API int dropkv_set_scorer(int mode);
 
+/* Test hook for the tensor-core scorer's failure path (process-wide, for the
+ * launches that follow).  wait_limit_ns: how long a wait on another warp role or
+ * another CTA may last before the kernel gives up, records a non-zero status word
+ * and runs to its end without further waits (0 = the default, 1 s).
+ * block_group_barrier != 0: each launch starts head 0's first group barrier
+ * below zero, so that barrier cannot complete and its wait runs out.  Nothing
+ * faults or traps: the launch ends with the status set, the call returns
+ * DROPKV_OK, and the next launch (hook off) is unaffected.  No counterpart in the
+ * reference. */
+DROPKV_API int dropkv_test_scorer_waits(uint64_t wait_limit_ns, int block_group_barrier);
+
 /* Byte offset, inside a dropkv_scores / dropkv_compress workspace, of the int32
  * device status word the tensor-core scorer writes (0 = every bounded wait
  * completed; non-zero = a wait timed out and the results are invalid).
@@ -110,7 +121,9 @@ DROPKV_API size_t dropkv_scores_status_offset(int dtype, int B, int Hq, int Hkv,
  * enter an allocator -- and so cannot provide the scratch dropkv_scores takes.
  * The scratch is a DROPKV_STATIC_SCRATCH_BYTES buffer compiled into the library
  * (one per device).  Arguments, results and errors as dropkv_scores, plus:
- *   - a problem whose scratch (dropkv_scores_workspace_size) exceeds the buffer
+ *   - the call is accepted when the scratch the scorer for this dtype needs fits
+ *     the buffer (dropkv_scores_workspace_size, the larger of the bf16 and fp32
+ *     needs, at most DROPKV_STATIC_SCRATCH_BYTES guarantees that); otherwise it
  *     returns DROPKV_ERR_WORKSPACE with a message naming both sizes, and
  *     launches nothing;
  *   - the first call on each device looks the buffer's address up (and, like
@@ -121,13 +134,25 @@ DROPKV_API size_t dropkv_scores_status_offset(int dtype, int B, int Hq, int Hkv,
  *     (cudaMemsetAsync) before each launch; the caller initialises nothing;
  *   - all calls on one device share the buffer: two calls whose work can overlap
  *     on the device (unordered streams, or several host threads) race on it and
- *     give wrong scores.  Order them (one stream, or events).
- * No counterpart in the reference, whose scorer allocates its intermediates on
- * every call (dropkv_triton.py:736-769). */
+ *     give wrong scores.  Order them (one stream, or events);
+ *   - the device status word of the call (non-zero: a bounded wait in the
+ *     tensor-core scorer timed out and the scores are invalid) lives in the
+ *     buffer; dropkv_scores_static_status copies it out.
+ * No counterpart in the reference. */
 DROPKV_API int dropkv_scores_static(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd,
                                     int Lq, const void* k, const void* v, int dtype, int B, int Hq, int Hkv,
                                     int Lk, int D, int window, float eps, int round_p, float* scores,
                                     void* stream);
+
+/* Copies, by an asynchronous copy on `stream`, the int32 device status word of
+ * the last dropkv_scores_static call on the current device for this problem
+ * (same dtype and sizes) to *status_out: device memory, or host memory the
+ * device can address (pinned).  0 = every bounded wait completed; problems on
+ * the CUDA-core scorer, which has no bounded waits, always read 0.  Enqueue it
+ * on the stream of that call, after it; allocates nothing.
+ * No counterpart in the reference. */
+DROPKV_API int dropkv_scores_static_status(int dtype, int B, int Hq, int Hkv, int Lk, int D, int window,
+                                           int* status_out, void* stream);
 
 /* Scratch bytes dropkv_select needs. */
 DROPKV_API size_t dropkv_select_workspace_size(int B, int Hkv, int Lk);

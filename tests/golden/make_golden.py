@@ -16,6 +16,18 @@ torch build), runs the reference's own functions on them and stores the outputs:
   same inputs (dropkv_cache.py:355-477, the reference's PyTorch eviction path)
 * ``kc_sum`` / ``vc_sum`` -- float64 sums of ``_gather_compressed`` outputs
   (dropkv_cache.py:479-491) as a compact check of the gather.
+* ``keep_idx_round`` / ``keep_idx_exact`` -- the reference's own selection
+  (``_compute_keep_indices`` with ``use_triton=True``: max_pool1d, protection,
+  topk, sort, dropkv_cache.py:462-477) applied to the scores of
+  ``dropkv_scores_reference`` with and without p rounded to the input dtype, i.e.
+  the kept sets the reference's Triton branch produces when its kernel returns
+  the reference formula's values (its tests hold the kernel to that function,
+  tests/test_dropkv_triton.py:122-137).  The scorer is put in place of
+  ``dropkv_scores_triton`` for the call, since the Triton kernel needs a GPU.
+  Where attention saturates (p ~ 1 in some window row) these sets and
+  ``keep_idx_cache`` differ: the score there is fp32 cancellation noise, and
+  each of the reference's paths keeps or evicts such a key by the sign of its
+  own noise.
 
 Inputs are not stored; their SHA-256 is, so a test can detect generator drift.
 """
@@ -113,6 +125,18 @@ def main():
         cache = dropkv_cache.DropKVCache(keep_ratio=wl.keep_ratio, window_size=W,
                                          kernel_size=wl.kernel_size, use_triton=False)
         idx = cache._compute_keep_indices(Q, K, V)
+        if wl.Lq >= W:
+            orig = dropkv_triton.dropkv_scores_triton
+            for field, rnd in (("keep_idx_round", True), ("keep_idx_exact", False)):
+                dropkv_triton.dropkv_scores_triton = (
+                    lambda q, k, v, window_size=8, _r=rnd: dropkv_triton.dropkv_scores_reference(
+                        q, k, v, window_size=window_size, match_pytorch_precision=_r))
+                try:
+                    sel = dropkv_cache.DropKVCache(keep_ratio=wl.keep_ratio, window_size=W,
+                                                   kernel_size=wl.kernel_size, use_triton=True)
+                    rec[field] = sel._compute_keep_indices(Q, K, V).numpy()
+                finally:
+                    dropkv_triton.dropkv_scores_triton = orig
         kc, vc = dropkv_cache.DropKVCache._gather_compressed(K, V, idx)
         rec["keep_idx_cache"] = idx.numpy()
         rec["kc_sum"] = np.float64(kc.double().sum().item())

@@ -120,3 +120,65 @@ def dilate(mask: np.ndarray, r: int) -> np.ndarray:
         out[..., s:] |= mask[..., :L - s]
         out[..., :L - s] |= mask[..., s:]
     return out
+
+
+def kept_set_report(idx_got: np.ndarray, idx_ref: np.ndarray, pooled_ref: np.ndarray,
+                    saturated: np.ndarray, radius: int, rel_band: float) -> dict:
+    """Classify every position in which two kept sets differ, row by row.
+
+    ``pooled_ref`` is the reference side's pooled score row, ``saturated`` marks
+    positions whose softmax probability reaches ILL_P in some window row (their
+    score is fp32 cancellation noise in the reference formula), ``radius`` the
+    pooling half-width.  Classes, in order of precedence:
+
+    * ``saturated_nbhd`` -- within ``radius`` of a saturated position (its pooled
+      value carries the noise);
+    * ``exact_tie``      -- pooled value equal to the row's keep threshold;
+    * ``displaced``      -- between the (k-n)-th and (k+n)-th largest pooled
+      values, n being the row's saturated-neighbourhood differences (each of those
+      moves the keep boundary by one);
+    * ``near_tie``       -- within ``rel_band`` (relative) of the threshold;
+    * ``unexplained``    -- anything else, listed as (row, index, value, threshold).
+    """
+    k = idx_ref.shape[-1]
+    near = dilate(saturated, radius)
+    rep = {"rows": 0, "kept": 0, "diff": 0, "saturated_positions": int(saturated.sum()),
+           "saturated_nbhd": 0, "exact_tie": 0, "displaced": 0, "near_tie": 0, "unexplained": []}
+    for row in np.ndindex(idx_ref.shape[:-1]):
+        d = set(np.asarray(idx_got[row]).tolist()) ^ set(np.asarray(idx_ref[row]).tolist())
+        rep["rows"] += 1
+        rep["kept"] += k
+        rep["diff"] += len(d)
+        if not d:
+            continue
+        p = pooled_ref[row]
+        srt = np.sort(p)[::-1]
+        thr = srt[k - 1]
+        n_sat = sum(1 for j in d if near[row][j])
+        hi = srt[max(0, k - 1 - n_sat)]
+        lo = srt[min(len(srt) - 1, k - 1 + n_sat)]
+        for j in d:
+            if near[row][j]:
+                rep["saturated_nbhd"] += 1
+            elif p[j] == thr:
+                rep["exact_tie"] += 1
+            elif n_sat and lo <= p[j] <= hi:
+                rep["displaced"] += 1
+            elif abs(float(p[j]) - float(thr)) <= rel_band * abs(float(thr)):
+                rep["near_tie"] += 1
+            else:
+                rep["unexplained"].append((row, int(j), float(p[j]), float(thr)))
+    return rep
+
+
+def assert_kept_report(rep: dict, radius: int, what: str, near_tie_frac: float = 2e-3):
+    """No unexplained difference; the excused ones bounded: a saturated position
+    flips at most its pooling neighbourhood in each set (2 (2 radius + 1)) and
+    displaces as many boundary positions; near-ties at most ``near_tie_frac`` of
+    the kept positions plus 4 per row."""
+    assert not rep["unexplained"], f"{what}: kept sets differ beyond the excused classes: {rep['unexplained'][:6]}"
+    cap = 2 * (2 * radius + 1) * rep["saturated_positions"]
+    assert rep["saturated_nbhd"] <= cap, f"{what}: {rep['saturated_nbhd']} saturated-neighbourhood differences > {cap}"
+    assert rep["displaced"] <= cap, f"{what}: {rep['displaced']} displaced boundary positions > {cap}"
+    ncap = near_tie_frac * rep["kept"] + 4 * rep["rows"]
+    assert rep["near_tie"] <= ncap, f"{what}: {rep['near_tie']} near-tie differences > {ncap:.0f}"

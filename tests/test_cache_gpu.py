@@ -11,8 +11,8 @@ import numpy as np
 import pytest
 import torch
 
-from parity import (DTYPE_NAME, dilate, golden_cases, input_digest, keep_set_mismatch, load_golden,
-                    well_conditioned)
+from parity import (DTYPE_NAME, assert_kept_report, dilate, golden_cases, input_digest, keep_set_mismatch,
+                    kept_set_report, load_golden, well_conditioned)
 from dropkv_b200 import DropKVCache, ops, prefill_chunked
 from dropkv_b200.workloads import Workload, make_qkv
 from oracle import dropkv_oracle as O
@@ -57,6 +57,38 @@ def test_compress_matches_reference_cache_path(name):
     ek = torch.gather(K, 2, it[..., None].expand(-1, -1, -1, wl.D))
     ev = torch.gather(V, 2, it[..., None].expand(-1, -1, -1, wl.D))
     assert torch.equal(kc.cpu(), ek) and torch.equal(vc.cpu(), ev)
+
+
+@pytest.mark.parametrize("name", golden_cases())
+def test_compress_matches_reference_selection(name):
+    """Against the kept sets of the reference's own selection on the reference
+    formula's scores with p rounded (keep_idx_round, the semantics of the
+    reference's Triton branch): every difference is classified and bounded
+    (parity.kept_set_report / assert_kept_report), with near-ties limited to the
+    score tolerance. On sink_bf16_4k the sink (key 0) is kept where all three of
+    the reference's paths keep it."""
+    z, wl = load_golden(name)
+    if "keep_idx_round" not in z.files:
+        pytest.skip("Lq < window: no reference scorer output")
+    Q, K, V = make_qkv(wl, "cpu")
+    W = wl.window_size
+    kl = z["keep_idx_round"].shape[-1]
+    idx, _, _ = ops.compress(Q.cuda(), K.cuda(), V.cuda(), W, wl.kernel_size, kl)
+    idx = idx.cpu().numpy()
+    Qn, Kn = Q.float().numpy(), K.float().numpy()
+    sat = O.max_attention(Qn, Kn, W) >= 0.99
+    pooled = O.pool_and_protect(z["scores_round"], wl.kernel_size, W)
+    rel = 1e-5 if wl.dtype == torch.float32 else 1e-2
+    rep = kept_set_report(idx, z["keep_idx_round"], pooled, sat, wl.kernel_size // 2, rel_band=rel)
+    print(f"\n[parity] {name} vs keep_idx_round: "
+          + str({k: v for k, v in rep.items() if k != "unexplained"}))
+    assert_kept_report(rep, wl.kernel_size // 2, name)
+    if name == "sink_bf16_4k":
+        paths = [z[f] for f in ("keep_idx_cache", "keep_idx_round", "keep_idx_exact")]
+        for h in range(wl.Hkv):
+            votes = {bool((p[0, h] == 0).any()) for p in paths}
+            if len(votes) == 1:
+                assert bool((idx[0, h] == 0).any()) == votes.pop(), f"head {h}: sink decision"
 
 
 def test_chunked_equals_single_pass_bitwise():

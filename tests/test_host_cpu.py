@@ -179,17 +179,24 @@ def test_prefill_chunked_cleans_up_after_failure(strategy):
     assert c._evict_use_seen_tokens is False and c._budget_max_kv_tokens is None
 
 
-def test_dynamic_cache_helpers():
+def test_layer_store_access_and_crop():
+    """Layer indexing, iteration and crop of the cache's own store."""
     Q, K, V = _mk(Lq=16, Lk=16)
-    c = dropkv_b200.DynamicCache()
+    c = DropKVCache(keep_ratio=0.5)
+    c._prefill_mode = "accumulate"
     c.update(None, K, V, 0)
     c.update(None, K[:, :, :4], V[:, :, :4], 0)
-    assert c.get_seq_length() == 20 and len(c) == 1
-    legacy = c.to_legacy_cache()
-    c2 = dropkv_b200.DynamicCache.from_legacy_cache(legacy)
-    assert torch.equal(c2.key_cache[0], c.key_cache[0])
-    c2.crop(10)
-    assert c2.get_seq_length() == 10
+    c.update(None, K, V, 1)
+    assert len(c) == 2 and c.get_seq_length() == 20
+    k0, v0 = c[0]
+    assert torch.equal(k0, torch.cat([K, K[:, :, :4]], dim=2))
+    assert [t[0].shape[2] for t in c] == [20, 16]
+    with pytest.raises(KeyError):
+        c[2]
+    c.crop(10)
+    assert c.get_seq_length() == 10 and c.key_cache[0].shape[2] == 10 and c.key_cache[1].shape[2] == 10
+    c.crop(-4)
+    assert c.get_seq_length() == 6 and c.value_cache[0].shape[2] == 6
 
 
 @pytest.mark.parametrize("storage", ["cat", "buffer"])

@@ -64,6 +64,55 @@ def test_oracle_selection_matches_reference_cache_path(name):
     assert Vc_t == pytest.approx(float(z["vc_sum"]), rel=1e-12, abs=1e-9)
 
 
+@pytest.mark.parametrize("field,sfield", [("keep_idx_round", "scores_round"), ("keep_idx_exact", "scores_exact")])
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_select_matches_reference_select(name, field, sfield):
+    """Given the reference's own scores, the oracle's pool / protect / top-k / sort
+    keeps exactly the positions the reference's selection keeps
+    (dropkv_cache.py:462-477); only the order of exact ties may differ."""
+    z, wl = load_golden(name)
+    if field not in z.files:
+        pytest.skip("Lq < window: no reference scorer output")
+    pooled = O.pool_and_protect(z[sfield], wl.kernel_size, wl.window_size)
+    kl = z[field].shape[-1]
+    idx = O.select_keep_indices(pooled, kl)
+    bad = keep_set_mismatch(idx, z[field], pooled)
+    assert not bad, f"{name}/{field}: kept sets differ beyond exact ties at {bad[:8]}"
+
+
+SINK_HEADS = 8
+
+
+def _keeps_key0(idx):
+    return [bool((idx[0, h] == 0).any()) for h in range(SINK_HEADS)]
+
+
+def test_reference_paths_disagree_only_where_attention_saturates():
+    """sink_bf16_4k: key 0 is an attention sink whose softmax probability is 1.0
+    (fp32) in some window row of every head.  There the weight (p/(1-p+eps))^2
+    reaches ~1e12 and multiplies a cancelled ||v - y||^2, so each of the
+    reference's own eviction paths scores the sink with its own fp32 noise
+    (dropkv_triton.py:88-106, dropkv_cache.py:431-460) and keeps or evicts it by
+    that noise's sign.  The paths agree everywhere else, up to the boundary
+    positions those decisions displace and the near-ties the cache path's bf16 y
+    moves (dropkv_cache.py:434)."""
+    z, wl, Q, K, V = _inputs("sink_bf16_4k")
+    pmax = O.max_attention(Q, K, wl.window_size)
+    sat = pmax >= 0.99
+    assert int(sat.sum()) == SINK_HEADS and sat[..., 0].all(), "exactly key 0 saturates in every head"
+    cache, rnd, exact = z["keep_idx_cache"], z["keep_idx_round"], z["keep_idx_exact"]
+    assert _keeps_key0(cache) == [False, True, True, True, True, False, True, True]
+    assert _keeps_key0(rnd) == [True, True, False, True, False, True, True, False]
+    assert _keeps_key0(exact) == [True, False, True, False, False, True, True, False]
+    # the sink's raw scores are noise of either sign, orders of magnitude above the rest
+    sr = z["scores_round"][0, :, 0]
+    assert (np.abs(sr) > 1e5).all() and (sr < 0).any() and (sr > 0).any()
+    near = dilate(sat, wl.kernel_size // 2)
+    pooled = O.pool_and_protect(z["scores_round"], wl.kernel_size, wl.window_size)
+    bad = keep_set_mismatch(rnd, cache, pooled, allowed=near, rel_band=2e-2)
+    assert not bad, f"round vs cache path differ away from the sink at {bad[:8]}"
+
+
 def test_select_breaks_ties_to_lower_index():
     pooled = np.array([[1.0, 2.0, 2.0, 2.0, 0.5, 2.0]], dtype=np.float32)
     assert O.select_keep_indices(pooled, 3).tolist() == [[1, 2, 3]]

@@ -106,3 +106,50 @@ def test_tensor_core_scorer_repeatable():
     a = ops.scores(Q, K, V, 8)
     b = ops.scores(Q, K, V, 8)
     assert torch.equal(a, b)
+
+
+def test_bounded_wait_timeout_sets_status_and_next_call_is_correct():
+    """The scorer's failure path, driven without any fault: the test hook shortens
+    the wait limit to 1 ms and makes head 0's first group barrier unreachable.
+    The barrier wait runs out, the kernel records a non-zero status word and ends
+    (the call itself returns DROPKV_OK); the Python layer turns the status into
+    DropKVError(ERR_DEVICE).  The next call, hook off, on the same GPU and
+    workspace sizes, gives the oracle's scores."""
+    wl = llama_layer(8192)
+    Q, K, V = (t.cuda() for t in make_qkv(wl, "cpu"))
+    lib = _lib.load()
+    B, Hq, Lq, D = Q.shape
+    Hkv, Lk = K.shape[1], K.shape[2]
+    ws = torch.zeros(lib.dropkv_scores_workspace_size(B, Hq, Hkv, Lk, D, 8), dtype=torch.uint8, device="cuda")
+    out = torch.empty(B, Hkv, Lk, device="cuda")
+    off = lib.dropkv_scores_status_offset(_lib.DTYPE_BF16, B, Hq, Hkv, Lk, D, 8)
+    assert off != _lib.NO_STATUS, "the tensor-core scorer serves this shape"
+
+    def call():
+        return lib.dropkv_scores(Q.data_ptr(), *Q.stride(), Lq, K.data_ptr(), V.data_ptr(), _lib.DTYPE_BF16,
+                                 B, Hq, Hkv, Lk, D, 8, 1e-6, _lib.ROUND_BF16, out.data_ptr(), ws.data_ptr(),
+                                 ws.numel(), torch.cuda.current_stream().cuda_stream)
+
+    _lib.check(lib.dropkv_test_scorer_waits(1_000_000, 1), "test hook")
+    try:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        assert call() == _lib.OK
+        t1.record()
+        torch.cuda.synchronize()
+        status = int(ws[off:off + 4].view(torch.int32).item())
+        assert status != 0, "the blocked barrier's wait must run out and set the status word"
+        assert t0.elapsed_time(t1) < 1000.0, "every wait gave up within its 1 ms limit"
+        with pytest.raises(_lib.DropKVError) as err:
+            ops.scores(Q, K, V, 8)  # DROPKV_CHECK_STATUS=1 (tests/conftest.py) reads the status
+        assert err.value.code == _lib.ERR_DEVICE
+    finally:
+        _lib.check(lib.dropkv_test_scorer_waits(0, 0), "test hook off")
+    assert call() == _lib.OK
+    torch.cuda.synchronize()
+    assert int(ws[off:off + 4].view(torch.int32).item()) == 0
+    Qn, Kn, Vn = (t.float().cpu().numpy() for t in (Q, K, V))
+    want = O.scores_reference(Qn, Kn, Vn, 8, round_p="bf16")
+    cond = well_conditioned(O.max_attention(Qn, Kn, 8))
+    assert_scores_close(out.cpu().numpy(), want, rtol=1e-2, atol=1e-3, mask=cond, what="after the timeout")
