@@ -4,34 +4,60 @@
 // which is what the model's attention computes over the cache DropKVCache.update
 // returns (dropkv_cache.py:609-617 append the token, the model's SDPA attends).
 //
-// With one to a few query rows per KV head the work is a matrix-vector product per
-// key: HBM-bound, no tensor-core tile to fill. One thread-block cluster of CL CTAs
-// per (sequence, KV head, block of up to MR query rows); CTA r takes a contiguous
-// range of keys. In each CTA a producer warp streams chunks of KC keys of K and V
-// (contiguous rows) into a 4-stage shared-memory ring with bulk copies on
-// mbarriers, and CW compute warps consume them (4 warps and 32-key chunks: small
-// CTAs, so that several share an SM and the clusters of a launch are resident
-// together): a key row is read by D/8 lanes,
-// 16 bytes each, every lane keeping the running max, sum and output of its 8
-// columns for each query row (softmax in base 2). The CTAs' partials (max, sum,
-// output) are merged through distributed shared memory in CTA order, each CTA
-// writing a slice of O. Every wait is bounded; a wait that gives up sets a bit in
-// the status word (the first 4 bytes of the workspace) and the kernel finishes.
-#include <cooperative_groups.h>
-
+// A handful of query rows per KV head make this an HBM-bound stream over K and V.
+// The keys of each (sequence, KV head, tile of 8 query rows) are split over CTAs
+// of 12 warps, one CTA per SM and all of them in one wave; each warp takes every
+// 12th step of 16 keys and keeps a running (max, sum, output) of its own. A
+// step's K rows are fetched for the next step as soon as its S is computed, its V
+// rows as soon as its P.V is issued, so every warp keeps a step of loads in
+// flight.
+//
+// Both products run on the tensor cores as m16n8k16 MMAs fed straight from
+// registers, so no shuffle reduction per key is needed:
+//   S  = Q K^T   A = the 8 query rows (rows 8..15 zero), B = K^T: 8 keys per MMA;
+//   O^T += V^T P^T   A = V^T (16 columns of D), B = P^T: the softmax weights of the
+//                    16 keys, taken from S's accumulator registers as they lie.
+// A dot product may sum its D terms in any order, so the D axis is permuted to
+// suit the loads: lane (gid, tig) of a warp (gid = lane / 4, tig = lane % 4) reads
+// the bytes [64 i + 16 tig, +16) of its key row for K (i < D / 32; four lanes
+// cover 64 contiguous bytes of a row) and the bytes [128 i + 16 gid, +16) of four
+// key rows for V (eight lanes cover 128 contiguous bytes), every load a 16-byte
+// vector of whole 32-byte sectors; the MMA's k-index pairs of Q use the same
+// permutation as those of K, and the output columns carry the V permutation back.
+//
+// The warps' partials are merged in shared memory; the CTAs of one tile write
+// theirs (output, max, sum) to the workspace, and the CTA that increments the
+// tile's counter last merges them (max-rescaled sum, loads batched), writes O and
+// resets the counter, so the workspace is left as it was found. No wait in this
+// kernel depends on another CTA.
 #include <algorithm>
+#include <atomic>
 #include <type_traits>
 
-#include "tc_common.cuh"
-
-namespace cg = cooperative_groups;
+#include "common.cuh"
 
 namespace dropkv {
 namespace {
 
-constexpr int DA_ST = 4;                 // ring stages
-constexpr int DA_MAXCL = 16;
-constexpr uint64_t DA_WAIT_NS = 1000000000ull;
+constexpr int DA_WARPS = 12;
+constexpr int DA_NT = 32 * DA_WARPS;
+constexpr int DA_KS = 16;              // keys per step (the k extent of the P.V MMA)
+constexpr int DA_ROWS = 8;             // query rows per tile (the n extent of the P.V MMA)
+constexpr int DA_MIN_STEPS = DA_WARPS; // key steps per CTA at least
+constexpr int DA_MAX_SPLITS = 256;
+constexpr int DA_BATCH = 8;            // partials read at once by the merge
+
+// Dynamic shared memory: the warps' partials, then the merge's factors and sums.
+template <int D>
+struct DaSmem {
+  static constexpr int WO = 0;                                   // float [WARPS][ROWS][D]
+  static constexpr int WM = WO + DA_WARPS * DA_ROWS * D * 4;     // float [WARPS][ROWS]
+  static constexpr int WL = WM + DA_WARPS * DA_ROWS * 4;         // float [WARPS][ROWS]
+  static constexpr int FAC = WL + DA_WARPS * DA_ROWS * 4;        // float [MAX_SPLITS][ROWS]
+  static constexpr int LS = FAC + DA_MAX_SPLITS * DA_ROWS * 4;   // float [MAX_SPLITS][ROWS]
+  static constexpr int RS = LS + DA_MAX_SPLITS * DA_ROWS * 4;    // float [ROWS]
+  static constexpr int BYTES = RS + DA_ROWS * 4 + 16;            // + the last-CTA flag
+};
 
 struct DaArgs {
   const void* q;
@@ -41,49 +67,54 @@ struct DaArgs {
   int64_t kv_sb, kv_sh;  // element strides of a sequence and a KV head; rows of D contiguous
   int Hq, Hkv, g, Lq, L;
   int M;                 // g * Lq query rows per (b, KV head)
-  int chunk;             // keys per CTA (a multiple of the kernel's KC)
+  int ntiles;            // tiles of 8 query rows per (b, KV head)
+  int splits;            // CTAs per tile
+  int steps;             // key steps per CTA
   float scale_log2;      // scale * log2(e)
-  int* status;
+  float* part;           // [tiles][splits][8][D + 4]: output, max, sum (rows of 16-byte multiples)
+  unsigned* counter;     // [tiles]
   void* out;             // [B, Hq, Lq, D]
 };
 
-// compute warps and keys per stage for MR query rows per CTA
-template <int MR>
-struct DaCfg {
-  static constexpr int CW = 4;
-  static constexpr int KC = 32;
-  static constexpr int NT = 32 * (CW + 1);  // + the producer warp
-};
+__device__ __forceinline__ uint4 ld_stream(const void* p) {  // read once: no L1 allocation
+  uint4 r;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
 
-template <int D, int MR, int EB>
-struct DaLay {
-  static constexpr int CW = DaCfg<MR>::CW, KC = DaCfg<MR>::KC;
-  static constexpr int HALF = KC * D * EB;               // K (or V) rows of a stage
-  static constexpr int STAGE = 2 * HALF;
-  static constexpr int RING = 0;
-  static constexpr int WACC = RING;                      // float [CW][MR][D], in the ring once drained
-  static_assert(CW * MR * D * 4 <= DA_ST * STAGE, "warp partials fit the ring");
-  static constexpr int QS = RING + DA_ST * STAGE;        // float [MR][D]
-  static constexpr int WML = QS + MR * D * 4;            // float [CW][MR][2]
-  static constexpr int PART = WML + CW * MR * 2 * 4;     // float [MR][D + 2]: this CTA's partial
-  static constexpr int BND = PART + MR * (D + 2) * 4;    // int [MR]
-  static constexpr int BAR = (BND + MR * 4 + 7) & ~7;    // full[DA_ST], empty[DA_ST]
-  static constexpr int BYTES = BAR + 2 * DA_ST * 8;
-};
+__device__ __forceinline__ float ex2(float x) {  // 2^x, hardware approximation; 2^-inf = 0
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <typename T>
-__device__ __forceinline__ void unpack8(const uint4& r, float* f) {
-  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-      f[2 * i] = __uint_as_float(w[i] << 16);
-      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-    } else {
-      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-      f[2 * i] = x.x;
-      f[2 * i + 1] = x.y;
-    }
+__device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+// two floats rounded to T, x in the low half
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float x, float y) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(x, y);
+    return *reinterpret_cast<uint32_t*>(&h);
   }
 }
 
@@ -94,305 +125,327 @@ __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return
 template <>
 __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
 
-__device__ __forceinline__ float ex2(float x) {  // 2^x, hardware approximation; 2^-inf = 0
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
+// Column of D held in 32-bit word w of a lane's K slab (lane group tig) and of its
+// V slab (lane group gid); the word's second element is the next column.
+template <int D>
+__device__ __forceinline__ int k_col(int tig, int w) { return 32 * (w >> 2) + 8 * tig + 2 * (w & 3); }
+template <int D>
+__device__ __forceinline__ int v_col(int gid, int w) { return 64 * (w >> 2) + 8 * gid + 2 * (w & 3); }
 
-template <int NTH>
-__device__ __forceinline__ void compute_sync() {  // the compute warps only
-  asm volatile("bar.sync 1, %0;" ::"r"(NTH) : "memory");
-}
+template <typename T, int D>
+__global__ void __launch_bounds__(DA_NT, 1) decode_attn_kernel(DaArgs a) {
+  constexpr int NK = D / 32;  // 16-byte loads per K row and lane
+  constexpr int KW = 4 * NK;  // K words per row and lane (two per QK^T k-step)
+  constexpr int NV = D / 64;  // 16-byte loads per V row and lane
+  constexpr int DT = D / 16;  // P.V MMAs per key step (16 columns of D each)
+  constexpr int PR = D + 4;   // floats per row of a partial
+  static_assert(DT == 4 * NV, "one V word per column tile");
+  using Sm = DaSmem<D>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  float(*wo)[DA_ROWS][D] = reinterpret_cast<float(*)[DA_ROWS][D]>(smem + Sm::WO);
+  float(*wm)[DA_ROWS] = reinterpret_cast<float(*)[DA_ROWS]>(smem + Sm::WM);
+  float(*wl)[DA_ROWS] = reinterpret_cast<float(*)[DA_ROWS]>(smem + Sm::WL);
+  float(*fac)[DA_ROWS] = reinterpret_cast<float(*)[DA_ROWS]>(smem + Sm::FAC);
+  float(*lsh)[DA_ROWS] = reinterpret_cast<float(*)[DA_ROWS]>(smem + Sm::LS);
+  float* rsum = reinterpret_cast<float*>(smem + Sm::RS);
+  int* last_cta = reinterpret_cast<int*>(smem + Sm::RS + DA_ROWS * 4);
 
-template <typename T, int D, int MR>
-__global__ void __launch_bounds__(DaCfg<MR>::NT, 1) decode_attn_kernel(DaArgs a) {
-  using Ly = DaLay<D, MR, (int)sizeof(T)>;
-  constexpr int DA_CW = DaCfg<MR>::CW, DA_KC = DaCfg<MR>::KC, DA_NT = DaCfg<MR>::NT;
-  constexpr int LPK = D / 8;           // lanes per key row
-  constexpr int KPW = 32 / LPK;        // keys per warp and load
-  constexpr int KPWS = DA_KC / DA_CW;  // keys per warp and stage
-  constexpr int U = KPWS / KPW;        // loads per warp and stage
-  static_assert(U >= 1 && KPWS % KPW == 0, "whole loads per warp");
-  extern __shared__ __align__(128) uint8_t smem[];
-  cg::cluster_group cluster = cg::this_cluster();
-  const int CL = (int)cluster.num_blocks(), cr = (int)cluster.block_rank();
-  const int bh = blockIdx.y, rb = blockIdx.z;
+  const int split = blockIdx.x, bh = blockIdx.y, tile = blockIdx.z;
   const int b = bh / a.Hkv, hkv = bh % a.Hkv;
-  const int m0 = rb * MR, mr = min(MR, a.M - m0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float* qs = reinterpret_cast<float*>(smem + Ly::QS);
-  float* wacc = reinterpret_cast<float*>(smem + Ly::WACC);
-  float* wml = reinterpret_cast<float*>(smem + Ly::WML);
-  float* part = reinterpret_cast<float*>(smem + Ly::PART);
-  int* bnd = reinterpret_cast<int*>(smem + Ly::BND);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Ly::BAR);
-  uint64_t* empty = full + DA_ST;
-  const int s0 = min(a.L, cr * a.chunk), s1 = min(a.L, s0 + a.chunk);
-  const int nch = (s1 - s0 + DA_KC - 1) / DA_KC;  // stages of this CTA's keys
+  const int gid = lane >> 2, tig = lane & 3;
+  const int m0 = tile * DA_ROWS, mvalid = min(DA_ROWS, a.M - m0);
   const T* kb = reinterpret_cast<const T*>(a.k) + b * a.kv_sb + hkv * a.kv_sh;
   const T* vb = reinterpret_cast<const T*>(a.v) + b * a.kv_sb + hkv * a.kv_sh;
+  const int j_begin = split * a.steps * DA_KS;
+  const int j_end = min(a.L, j_begin + a.steps * DA_KS);
 
-  if (tid == 0) {
-    for (int st = 0; st < DA_ST; ++st) {
-      tc::mbar_init(&full[st], 1);
-      tc::mbar_init(&empty[st], DA_CW);
+  // query row gid of the tile, in the K permutation: qa[w] holds columns
+  // k_col(tig, w) and k_col(tig, w) + 1
+  uint32_t qa[KW];
+  int bound = -1;  // last key this row sees (-1: a padding row)
+  {
+    const int m = m0 + gid;
+    if (gid < mvalid) {
+      const int h = hkv * a.g + m / a.Lq, qi = m % a.Lq;
+      bound = a.L - a.Lq + qi;
+      const uint16_t* qp = reinterpret_cast<const uint16_t*>(a.q) + b * a.q_sb + h * a.q_sh + qi * a.q_ss;
+#pragma unroll
+      for (int w = 0; w < KW; ++w) {
+        const int d = k_col<D>(tig, w);
+        qa[w] = (uint32_t)qp[d * a.q_sd] | ((uint32_t)qp[(d + 1) * a.q_sd] << 16);
+      }
+    } else {
+#pragma unroll
+      for (int w = 0; w < KW; ++w) qa[w] = 0u;
     }
-    tc::fence_mbar_init();
+  }
+
+  float o[DT][4];
+#pragma unroll
+  for (int t = 0; t < DT; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+  float mrun = -INFINITY, lrun = 0.f;  // row gid: running max (base 2) and this lane's share of the sum
+
+  // K rows j0 + gid and j0 + 8 + gid (this lane's slab of each), V rows
+  // j0 + 2 tig + {0, 1, 8, 9} (this lane's columns of each); rows past the CTA's
+  // keys read as zeros
+  uint4 kr[2][NK], vr[4][NV];
+  auto load_k = [&](int j0) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int j = j0 + 8 * nt + gid;
+#pragma unroll
+      for (int i = 0; i < NK; ++i)
+        kr[nt][i] = j < j_end ? ld_stream(kb + (int64_t)j * D + 32 * i + 8 * tig) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  auto load_v = [&](int j0) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int j = j0 + 2 * tig + (r & 1) + 8 * (r >> 1);
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        vr[r][i] = j < j_end ? ld_stream(vb + (int64_t)j * D + 64 * i + 8 * gid) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  const int jstep = DA_WARPS * DA_KS;
+  int j0 = j_begin + warp * DA_KS;
+  if (j0 < j_end) {
+    load_k(j0);
+    load_v(j0);
+  }
+  for (; j0 < j_end; j0 += jstep) {
+    const int jn = j0 + jstep;
+    // S = Q K^T for the 16 keys: s[nt][e] = S[row gid][key j0 + 8 nt + 2 tig + e] (e < 2)
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      const uint32_t* kw = reinterpret_cast<const uint32_t*>(kr[nt]);
+#pragma unroll
+      for (int ks = 0; ks < KW / 2; ++ks) mma16816<T>(s[nt], qa[2 * ks], 0u, qa[2 * ks + 1], 0u, kw[2 * ks], kw[2 * ks + 1]);
+    }
+    if (jn < j_end) load_k(jn);  // the next step's K, in flight during this step's softmax and P.V
+    // online softmax of row gid (base 2); masked keys get -inf, hence weight 0
+    float x[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = j0 + 8 * (e >> 1) + 2 * tig + (e & 1);
+      x[e] = (j < j_end && j <= bound) ? s[e >> 1][e & 1] * a.scale_log2 : -INFINITY;
+    }
+    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mnew = fmaxf(mrun, mx);
+    const float muse = mnew == -INFINITY ? 0.f : mnew;
+    const float alpha = ex2(mrun - muse);
+    float p[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) p[e] = ex2(x[e] - muse);
+    lrun = lrun * alpha + ((p[0] + p[1]) + (p[2] + p[3]));
+    mrun = mnew;
+    // this lane's output columns belong to rows 2 tig and 2 tig + 1
+    const float a_lo = __shfl_sync(0xffffffffu, alpha, 8 * tig);
+    const float a_hi = __shfl_sync(0xffffffffu, alpha, 8 * tig + 4);
+    const uint32_t pb0 = pack2<T>(p[0], p[1]), pb1 = pack2<T>(p[2], p[3]);
+    uint32_t va[DT][4];  // A = V^T: rows v_col(gid, t) and v_col(gid, t) + 1, keys 2 tig + {0, 1, 8, 9}
+    {
+      const uint32_t* v0 = reinterpret_cast<const uint32_t*>(vr[0]);
+      const uint32_t* v1 = reinterpret_cast<const uint32_t*>(vr[1]);
+      const uint32_t* v2 = reinterpret_cast<const uint32_t*>(vr[2]);
+      const uint32_t* v3 = reinterpret_cast<const uint32_t*>(vr[3]);
+#pragma unroll
+      for (int t = 0; t < DT; ++t) {
+        va[t][0] = __byte_perm(v0[t], v1[t], 0x5410);
+        va[t][1] = __byte_perm(v0[t], v1[t], 0x7632);
+        va[t][2] = __byte_perm(v2[t], v3[t], 0x5410);
+        va[t][3] = __byte_perm(v2[t], v3[t], 0x7632);
+      }
+    }
+    if (jn < j_end) load_v(jn);  // the next step's V
+#pragma unroll
+    for (int t = 0; t < DT; ++t) {
+      o[t][0] *= a_lo;
+      o[t][1] *= a_hi;
+      o[t][2] *= a_lo;
+      o[t][3] *= a_hi;
+      mma16816<T>(o[t], va[t][0], va[t][1], va[t][2], va[t][3], pb0, pb1);
+    }
+  }
+
+  // ---- the CTA's partial: warps merged through shared memory -----------------
+  lrun += __shfl_xor_sync(0xffffffffu, lrun, 1);
+  lrun += __shfl_xor_sync(0xffffffffu, lrun, 2);
+  if (tig == 0) {
+    wm[warp][gid] = mrun;
+    wl[warp][gid] = lrun;
+  }
+#pragma unroll
+  for (int t = 0; t < DT; ++t) {
+    const int d = v_col<D>(gid, t);
+    wo[warp][2 * tig][d] = o[t][0];
+    wo[warp][2 * tig + 1][d] = o[t][1];
+    wo[warp][2 * tig][d + 1] = o[t][2];
+    wo[warp][2 * tig + 1][d + 1] = o[t][3];
   }
   __syncthreads();
-
-  if (warp == DA_CW) {
-    // ---- producer: K and V rows of each chunk of keys into the ring ----------
-    if (lane == 0) {
-      int c = 0;
-      for (; c < nch; ++c) {
-        const int st = c % DA_ST;
-        if (c >= DA_ST && !tc::mbar_wait(&empty[st], ((c / DA_ST) - 1) & 1, DA_WAIT_NS)) {
-          atomicOr(a.status, 1);
-          break;
-        }
-        const int j0 = s0 + c * DA_KC, nk = min(DA_KC, s1 - j0);
-        const uint32_t bytes = (uint32_t)(nk * D * (int)sizeof(T));
-        tc::mbar_arrive_expect_tx(&full[st], 2 * bytes);
-        tc::bulk_load(smem + Ly::RING + st * Ly::STAGE, kb + (int64_t)j0 * D, bytes, &full[st]);
-        tc::bulk_load(smem + Ly::RING + st * Ly::STAGE + Ly::HALF, vb + (int64_t)j0 * D, bytes, &full[st]);
-      }
-      // the CTA stays alive until every issued copy has landed
-      for (int j = max(0, c - DA_ST); j < c; ++j)
-        if (!tc::mbar_wait(&full[j % DA_ST], (j / DA_ST) & 1, DA_WAIT_NS)) atomicOr(a.status, 4);
+  if (tid < DA_ROWS) {  // per row: the warps' factors (fac[w][r]), the CTA's max and sum
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < DA_WARPS; ++w) mm = fmaxf(mm, wm[w][tid]);
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < DA_WARPS; ++w) {
+      const float f = mm == -INFINITY ? 0.f : ex2(wm[w][tid] - mm);
+      fac[w][tid] = f;
+      l = fmaf(f, wl[w][tid], l);
     }
-  } else {
-    // ---- compute warps --------------------------------------------------------
-    // query rows m0 .. m0 + mr - 1 of the group: row m is head hkv * g + m / Lq at
-    // query position m % Lq; pre-scaled so that logits come out in base 2
-    const T* qp = reinterpret_cast<const T*>(a.q);
-    for (int i = tid; i < MR * D; i += DA_CW * 32) {
-      const int rr = i / D, d = i % D, m = m0 + rr;
-      float x = 0.f;
-      if (rr < mr) {
-        const int h = hkv * a.g + m / a.Lq, qi = m % a.Lq;
-        x = to_f(qp[b * a.q_sb + h * a.q_sh + qi * a.q_ss + d * a.q_sd]) * a.scale_log2;
-      }
-      qs[rr * D + d] = x;
-    }
-    if (tid < MR) bnd[tid] = (tid < mr) ? a.L - a.Lq + (m0 + tid) % a.Lq : -1;
-    compute_sync<DA_CW * 32>();
-    const int dl = (lane % LPK) * 8;  // this lane's 8 columns
-    float qr[MR][8];
-#pragma unroll
-    for (int rr = 0; rr < MR; ++rr)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) qr[rr][e] = qs[rr * D + dl + e];
-    int bl[MR];
-#pragma unroll
-    for (int rr = 0; rr < MR; ++rr) bl[rr] = bnd[rr];
-    float mrun[MR], lrun[MR], acc[MR][8];
-#pragma unroll
-    for (int rr = 0; rr < MR; ++rr) {
-      mrun[rr] = -INFINITY;
-      lrun[rr] = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[rr][e] = 0.f;
-    }
-    for (int c = 0; c < nch; ++c) {
-      const int st = c % DA_ST;
-      if (!tc::mbar_wait(&full[st], (c / DA_ST) & 1, DA_WAIT_NS)) {
-        atomicOr(a.status, 2);
-        break;
-      }
-      const T* ks = reinterpret_cast<const T*>(smem + Ly::RING + st * Ly::STAGE);
-      const T* vs = reinterpret_cast<const T*>(smem + Ly::RING + st * Ly::STAGE + Ly::HALF);
-      const int j0 = s0 + c * DA_KC;
-      uint4 kr[U], vr[U];
-      int jj[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int kk = warp * KPWS + u * KPW + lane / LPK;
-        jj[u] = j0 + kk;
-        if (jj[u] < s1) {
-          kr[u] = *reinterpret_cast<const uint4*>(ks + kk * D + dl);
-          vr[u] = *reinterpret_cast<const uint4*>(vs + kk * D + dl);
-        } else {  // past this CTA's keys: the slot holds stale rows
-          kr[u] = make_uint4(0u, 0u, 0u, 0u);
-          vr[u] = kr[u];
-        }
-      }
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&empty[st]);  // this warp is done with the stage
-      float s[U][MR];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        float kf[8];
-        unpack8<T>(kr[u], kf);
-#pragma unroll
-        for (int rr = 0; rr < MR; ++rr) {
-          float t = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) t = fmaf(qr[rr][e], kf[e], t);
-          s[u][rr] = t;
-        }
-      }
-      // full dot products: sum over the LPK lanes of each key
-#pragma unroll
-      for (int o = LPK / 2; o >= 1; o >>= 1)
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-#pragma unroll
-          for (int rr = 0; rr < MR; ++rr) s[u][rr] += __shfl_xor_sync(0xffffffffu, s[u][rr], o);
-#pragma unroll
-      for (int rr = 0; rr < MR; ++rr) {
-        float cm = -INFINITY;
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          if (jj[u] >= s1 || jj[u] > bl[rr]) s[u][rr] = -INFINITY;
-          cm = fmaxf(cm, s[u][rr]);
-        }
-#pragma unroll
-        for (int o = LPK; o < 32; o <<= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
-        const float mn = fmaxf(mrun[rr], cm);
-        if (mn == -INFINITY) continue;  // nothing visible to this row yet (warp-uniform)
-        const float sc = ex2(mrun[rr] - mn);
-        mrun[rr] = mn;
-        lrun[rr] *= sc;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[rr][e] *= sc;
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const float p = ex2(s[u][rr] - mn);
-          if (lane % LPK == 0) lrun[rr] += p;  // one lane per key counts it
-          float vf[8];
-          unpack8<T>(vr[u], vf);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[rr][e] = fmaf(p, vf[e], acc[rr][e]);
-        }
-      }
-    }
-    // sum over the warp's keys (lanes with the same columns), then over the warps;
-    // the ring is free once every warp is past its last stage
-    compute_sync<DA_CW * 32>();
-#pragma unroll
-    for (int rr = 0; rr < MR; ++rr) {
-#pragma unroll
-      for (int o = LPK; o < 32; o <<= 1) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[rr][e] += __shfl_xor_sync(0xffffffffu, acc[rr][e], o);
-      }
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) lrun[rr] += __shfl_xor_sync(0xffffffffu, lrun[rr], o);
-      if (lane < LPK) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) wacc[(warp * MR + rr) * D + dl + e] = acc[rr][e];
-      }
-      if (lane == 0) {
-        wml[(warp * MR + rr) * 2] = mrun[rr];
-        wml[(warp * MR + rr) * 2 + 1] = lrun[rr];
-      }
-    }
-    compute_sync<DA_CW * 32>();
-    // this CTA's partial: max-rescaled sum of the warps'
-    for (int i = tid; i < MR * D; i += DA_CW * 32) {
-      const int rr = i / D, d = i % D;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < DA_CW; ++w) mx = fmaxf(mx, wml[(w * MR + rr) * 2]);
-      float o = 0.f, l = 0.f;
-      if (mx != -INFINITY) {
-#pragma unroll
-        for (int w = 0; w < DA_CW; ++w) {
-          const float f = ex2(wml[(w * MR + rr) * 2] - mx);
-          o = fmaf(f, wacc[(w * MR + rr) * D + d], o);
-          l = fmaf(f, wml[(w * MR + rr) * 2 + 1], l);
-        }
-      }
-      part[rr * (D + 2) + d] = o;
-      if (d == 0) {
-        part[rr * (D + 2) + D] = mx;
-        part[rr * (D + 2) + D + 1] = l;
-      }
-    }
+    lsh[0][tid] = mm;
+    rsum[tid] = l;
   }
-  cluster.sync();  // every CTA's partial is complete
-  // ---- merge in CTA order: this CTA writes elements [e0, e1) of the mr x D block --
-  const int E = mr * D;
-  const int e0 = (int)(((long long)cr * E) / CL), e1 = (int)(((long long)(cr + 1) * E) / CL);
+  __syncthreads();
+  const int tile_id = bh * a.ntiles + tile;
   T* op = reinterpret_cast<T*>(a.out);
-  for (int e = e0 + tid; e < e1; e += DA_NT) {
-    const int rr = e / D, d = e % D;
-    float mx = -INFINITY;
-    for (int c2 = 0; c2 < CL; ++c2) mx = fmaxf(mx, cluster.map_shared_rank(part, c2)[rr * (D + 2) + D]);
-    float o = 0.f, l = 0.f;
-    if (mx != -INFINITY) {
-      for (int c2 = 0; c2 < CL; ++c2) {
-        const float* pr = cluster.map_shared_rank(part, c2) + rr * (D + 2);
-        const float ms = pr[D];
-        if (ms == -INFINITY) continue;
-        const float f = ex2(ms - mx);
-        o = fmaf(f, pr[d], o);
-        l = fmaf(f, pr[D + 1], l);
+  auto out_at = [&](int r, int d) -> T* {
+    const int m = m0 + r, h = hkv * a.g + m / a.Lq, qi = m % a.Lq;
+    return op + (((size_t)b * a.Hq + h) * a.Lq + qi) * D + d;
+  };
+  auto cta_out = [&](int r, int d) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < DA_WARPS; ++w) acc = fmaf(fac[w][r], wo[w][r][d], acc);
+    return acc;
+  };
+  if (a.splits == 1) {  // the only CTA of the tile: O directly
+    for (int e = tid; e < mvalid * D; e += DA_NT) {
+      const int r = e / D, d = e % D;
+      *out_at(r, d) = from_f<T>(rsum[r] > 0.f ? cta_out(r, d) / rsum[r] : 0.f);
+    }
+    return;
+  }
+  float* pp = a.part + ((size_t)tile_id * a.splits + split) * DA_ROWS * PR;
+  for (int e = tid; e < mvalid * D; e += DA_NT) {
+    const int r = e / D, d = e % D;
+    pp[r * PR + d] = cta_out(r, d);
+  }
+  if (tid < mvalid) {
+    pp[tid * PR + D] = lsh[0][tid];
+    pp[tid * PR + D + 1] = rsum[tid];
+  }
+  // ---- the last CTA of the tile merges every partial ---------------------------
+  __threadfence();  // this CTA's partial is visible before its arrival is counted
+  __syncthreads();
+  if (tid == 0) *last_cta = atomicAdd(&a.counter[tile_id], 1u) == (unsigned)(a.splits - 1);
+  __syncthreads();
+  if (!*last_cta) return;
+  __threadfence();
+  const float* pt = a.part + (size_t)tile_id * a.splits * DA_ROWS * PR;
+  // (a) every partial's max and sum into shared memory
+  for (int i = tid; i < a.splits * mvalid; i += DA_NT) {
+    const int s2 = i / mvalid, r = i % mvalid;
+    const float* ps = pt + ((size_t)s2 * DA_ROWS + r) * PR + D;
+    fac[s2][r] = __ldcg(ps);
+    lsh[s2][r] = __ldcg(ps + 1);
+  }
+  __syncthreads();
+  // (b) one warp per row: the row's max, each partial's factor, the total sum
+  if (warp < mvalid) {
+    const int r = warp;
+    float mm = -INFINITY;
+    for (int s2 = lane; s2 < a.splits; s2 += 32) mm = fmaxf(mm, fac[s2][r]);
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o2));
+    float l = 0.f;
+    for (int s2 = lane; s2 < a.splits; s2 += 32) {
+      const float f = mm == -INFINITY ? 0.f : ex2(fac[s2][r] - mm);
+      fac[s2][r] = f;
+      l = fmaf(f, lsh[s2][r], l);
+    }
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o2);
+    if (lane == 0) rsum[r] = l;
+  }
+  __syncthreads();
+  // (c) O, four columns per thread, DA_BATCH partials loaded at a time
+  for (int e = tid; e < mvalid * (D / 4); e += DA_NT) {
+    const int r = e / (D / 4), d = 4 * (e % (D / 4));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < a.splits; s0 += DA_BATCH) {
+      float4 vv[DA_BATCH];
+#pragma unroll
+      for (int u = 0; u < DA_BATCH; ++u)
+        vv[u] = s0 + u < a.splits
+                    ? __ldcg(reinterpret_cast<const float4*>(pt + ((size_t)(s0 + u) * DA_ROWS + r) * PR + d))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < DA_BATCH; ++u) {
+        const float f = s0 + u < a.splits ? fac[s0 + u][r] : 0.f;
+        acc.x = fmaf(f, vv[u].x, acc.x);
+        acc.y = fmaf(f, vv[u].y, acc.y);
+        acc.z = fmaf(f, vv[u].z, acc.z);
+        acc.w = fmaf(f, vv[u].w, acc.w);
       }
     }
-    const int m = m0 + rr, h = hkv * a.g + m / a.Lq, qi = m % a.Lq;
-    op[(((size_t)b * a.Hq + h) * a.Lq + qi) * D + d] = from_f<T>(l > 0.f ? o / l : 0.f);
+    const float inv = rsum[r] > 0.f ? 1.f / rsum[r] : 0.f;
+    T* dst = out_at(r, d);
+    dst[0] = from_f<T>(acc.x * inv);
+    dst[1] = from_f<T>(acc.y * inv);
+    dst[2] = from_f<T>(acc.z * inv);
+    dst[3] = from_f<T>(acc.w * inv);
   }
-  cluster.sync();  // keep this CTA's partial alive until the cluster has read it
+  if (tid == 0) a.counter[tile_id] = 0u;  // ready for the next launch on this workspace
 }
 
 using DaKernel = void (*)(DaArgs);
 
-template <typename T, int D>
-DaKernel pick_da(int mr, int* smem) {
-  constexpr int EB = (int)sizeof(T);
-  switch (mr) {
-    case 1: *smem = DaLay<D, 1, EB>::BYTES; return decode_attn_kernel<T, D, 1>;
-    case 2: *smem = DaLay<D, 2, EB>::BYTES; return decode_attn_kernel<T, D, 2>;
-    case 4: *smem = DaLay<D, 4, EB>::BYTES; return decode_attn_kernel<T, D, 4>;
-    default: *smem = DaLay<D, 8, EB>::BYTES; return decode_attn_kernel<T, D, 8>;
-  }
-}
-
-int da_threads(int mr) { return mr <= 4 ? DaCfg<4>::NT : DaCfg<8>::NT; }
-int da_keys_per_stage(int mr) { return mr <= 4 ? DaCfg<4>::KC : DaCfg<8>::KC; }
-
-// Clusters of `cl` CTAs that can be resident at once (a cluster must fit in one
-// GPC, and GPCs differ in size), cached per device, kernel variant and size.
-int da_active_clusters(DaKernel kern, int var, int cl, int threads, int smem) {
-  static std::atomic<int> cache[16][DA_MAXCL + 1][16];  // zero: not queried yet
+int da_num_sms() {
+  static std::atomic<int> cache[64];  // zero: not queried yet
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 16) {
-    const int c = cache[var][cl][dev].load(std::memory_order_relaxed);
+  if (dev >= 0 && dev < 64) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
     if (c > 0) return c;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(cl);
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cl;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+  int n = 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) {
     cudaGetLastError();
-    return 1 << 20;
+    n = 148;
   }
-  if (dev >= 0 && dev < 16) cache[var][cl][dev].store(n, std::memory_order_relaxed);
+  if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
   return n;
+}
+
+struct DaPlan {
+  int ntiles, tiles, splits, steps;
+  size_t off_counter, off_part, bytes;
+};
+
+// CTAs per tile: as many as keep the launch to one CTA per SM (one wave), each
+// with at least DA_MIN_STEPS key steps; the last CTA never starts empty.
+DaPlan plan_da(int B, int Hkv, int M, int L, int D) {
+  DaPlan p;
+  p.ntiles = (M + DA_ROWS - 1) / DA_ROWS;
+  p.tiles = B * Hkv * p.ntiles;
+  const int nsteps = (L + DA_KS - 1) / DA_KS;
+  int splits = std::max(1, std::min(da_num_sms() / p.tiles, (nsteps + DA_MIN_STEPS - 1) / DA_MIN_STEPS));
+  splits = std::min(splits, DA_MAX_SPLITS);
+  p.steps = (nsteps + splits - 1) / splits;
+  p.splits = (nsteps + p.steps - 1) / p.steps;
+  p.off_counter = 256;  // the first 256 bytes: the status word (always zero here)
+  p.off_part = align_up(p.off_counter + (size_t)p.tiles * 4, 256);
+  p.bytes = p.splits > 1 ? p.off_part + (size_t)p.tiles * p.splits * DA_ROWS * (D + 4) * 4 : p.off_part;
+  return p;
 }
 
 }  // namespace
 
-size_t decode_attention_workspace_size(int, int, int, int, int, int) { return 256; }  // the status word
+size_t decode_attention_workspace_size(int B, int Hq, int Hkv, int Lq, int L, int D) {
+  return plan_da(B, Hkv, (Hq / Hkv) * Lq, L, D).bytes;
+}
 
 int launch_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
                             const void* k, const void* v, int64_t kv_sb, int64_t kv_sh, int dtype, int B, int Hq,
                             int Hkv, int L, int D, float scale, void* out, void* ws, cudaStream_t st) {
-  int dev = 0;
-  cudaGetDevice(&dev);
   DaArgs a;
   a.q = q;
   a.q_sb = q_sb;
@@ -409,59 +462,35 @@ int launch_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q
   a.Lq = Lq;
   a.L = L;
   a.M = a.g * Lq;
-  const int mr = a.M <= 1 ? 1 : (a.M <= 2 ? 2 : (a.M <= 4 ? 4 : 8));
-  const int nrb = (a.M + mr - 1) / mr;
-  int smem = 0, var;
+  const DaPlan p = plan_da(B, Hkv, a.M, L, D);
+  if (p.ntiles > 65535) return fail(DROPKV_ERR_UNSUPPORTED, "decode attention: %d query rows per KV head", a.M);
+  a.ntiles = p.ntiles;
+  a.splits = p.splits;
+  a.steps = p.steps;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.counter = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + p.off_counter);
+  a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.off_part);
+  a.out = out;
   DaKernel kern;
-  if (dtype == DROPKV_DTYPE_BF16) {
-    kern = D == 128 ? pick_da<__nv_bfloat16, 128>(mr, &smem) : pick_da<__nv_bfloat16, 64>(mr, &smem);
-    var = D == 128 ? 0 : 4;
-  } else {
-    kern = D == 128 ? pick_da<__half, 128>(mr, &smem) : pick_da<__half, 64>(mr, &smem);
-    var = D == 128 ? 8 : 12;
-  }
-  var += mr == 1 ? 0 : (mr == 2 ? 1 : (mr == 4 ? 2 : 3));
-  static DeviceOnce done[16];  // attributes set, per variant and device
+  const int var = (dtype == DROPKV_DTYPE_BF16 ? 0 : 2) + (D == 128 ? 0 : 1);
+  if (dtype == DROPKV_DTYPE_BF16)
+    kern = D == 128 ? decode_attn_kernel<__nv_bfloat16, 128> : decode_attn_kernel<__nv_bfloat16, 64>;
+  else
+    kern = D == 128 ? decode_attn_kernel<__half, 128> : decode_attn_kernel<__half, 64>;
+  const int smem = D == 128 ? DaSmem<128>::BYTES : DaSmem<64>::BYTES;
+  static DeviceOnce done[4];  // shared-memory attribute set, per variant and device
+  int dev = 0;
+  cudaGetDevice(&dev);
   if (!done[var].done(dev)) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
-        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-      return fail(DROPKV_ERR_CUDA, "cannot set decode attention kernel attributes");
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return fail(DROPKV_ERR_CUDA, "cannot set decode attention shared memory size %d", smem);
     done[var].mark(dev);
   }
-  // CTAs per cluster: the size that finishes soonest, counting the waves the
-  // launch's clusters need and the key stages each CTA streams; at most 16
-  const int rows = B * Hkv * nrb;
-  const int kc = da_keys_per_stage(mr), threads = da_threads(mr);
-  int cl = 1, chunk = ((L + kc - 1) / kc) * kc;
-  double best = 1e30;
-  for (int c = std::min(DA_MAXCL, (L + kc - 1) / kc); c >= 1; c /= 2) {
-    int ch = (L + c - 1) / c;
-    ch = ((ch + kc - 1) / kc) * kc;
-    const int cc = (L + ch - 1) / ch;  // every CTA gets keys
-    const int act = da_active_clusters(kern, var, cc, threads, smem);
-    const double t = (double)((rows + act - 1) / act) * (ch / kc + 2);  // + merge and launch, in stages
-    if (t < best - 1e-9) {
-      best = t;
-      cl = cc;
-      chunk = ch;
-    }
-  }
-  a.chunk = chunk;
-  a.scale_log2 = scale * 1.4426950408889634f;
-  a.status = reinterpret_cast<int*>(ws);
-  a.out = out;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(cl, B * Hkv, nrb);
-  cfg.blockDim = dim3(da_threads(mr));
+  cfg.gridDim = dim3(p.splits, B * Hkv, p.ntiles);
+  cfg.blockDim = dim3(DA_NT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cl;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
   if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "decode attention launch: %s", cudaGetErrorString(e));
   return check_launch("decode_attention");
