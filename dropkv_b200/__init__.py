@@ -11,6 +11,9 @@ Public API (the reference's names and semantics):
   the stages as tensor functions over the C ABI (include/dropkv_b200.h);
   ``Compressor`` (pre-planned, allocation-free calls) and ``HostPipeline``
   (host-resident layers with overlapped copies).
+* ``compress_varlen`` / ``VarlenCompressor``: a ragged batch of sequences in one
+  call, keep_len per sequence evaluated on the device (total_tokens /
+  max_keep_len per sequence).
 * ``dropkv_b200.hf`` (imported on demand, needs transformers): the
   Transformers integration -- ``DropKVCache(config, ...)``, query-state
   plumbing, decode attention over the compressed cache, generate wiring.
@@ -18,8 +21,8 @@ Public API (the reference's names and semantics):
 
 from ._lib import DropKVError, version
 from .cache import DropKVCache, prefill_chunked
-from .ops import (Compressor, HostPipeline, compress, decode_attention, dropkv_scores_cuda,
-                  gather_compressed, scores, select_keep_indices)
+from .ops import (Compressor, HostPipeline, VarlenCompressor, compress, compress_varlen, decode_attention,
+                  dropkv_scores_cuda, gather_compressed, scores, select_keep_indices)
 
 # Name of the reference entry point (dropkv_triton.py:643) for drop-in imports.
 dropkv_scores_triton = dropkv_scores_cuda
@@ -27,5 +30,5 @@ dropkv_scores_triton = dropkv_scores_cuda
 __all__ = [
     "DropKVCache", "prefill_chunked", "DropKVError", "version",
     "compress", "decode_attention", "dropkv_scores_cuda", "dropkv_scores_triton", "gather_compressed",
-    "scores", "select_keep_indices", "Compressor", "HostPipeline",
+    "scores", "select_keep_indices", "Compressor", "HostPipeline", "VarlenCompressor", "compress_varlen",
 ]

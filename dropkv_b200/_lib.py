@@ -19,6 +19,16 @@ OK, ERR_ARG, ERR_WORKSPACE, ERR_CUDA, ERR_UNSUPPORTED, ERR_DEVICE = range(6)
 
 _c_int, _c_i64, _c_f, _c_sz, _c_p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
 
+VARLEN_MAX_SEQS = 32
+
+
+class VarlenSeq(ctypes.Structure):
+    """``dropkv_varlen_seq``: one sequence of a ragged batch (include/dropkv_b200.h)."""
+    _fields_ = [("q", _c_p), ("q_sb", _c_i64), ("q_sh", _c_i64), ("q_ss", _c_i64), ("q_sd", _c_i64),
+                ("Lq", _c_int), ("B", _c_int), ("Lk", _c_int), ("cap", _c_int),
+                ("k", _c_p), ("v", _c_p), ("keep_idx", _c_p), ("k_out", _c_p), ("v_out", _c_p)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "dropkv_version": (ctypes.c_char_p, []),
@@ -57,6 +67,11 @@ SIGNATURES = {
                                  _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int,
                                  _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz,
                                  _c_p]),
+    "dropkv_compress_varlen_workspace_size": (_c_sz, [_c_int, ctypes.POINTER(VarlenSeq), _c_int, _c_int, _c_int,
+                                                      _c_int]),
+    "dropkv_compress_varlen": (_c_int, [_c_int, ctypes.POINTER(VarlenSeq), _c_int, _c_int, _c_int, _c_int, _c_int,
+                                        _c_f, _c_int, _c_int, _c_int, ctypes.c_double, _c_int, _c_p, _c_p, _c_p,
+                                        _c_p, _c_sz, _c_p]),
 }
 
 

@@ -120,7 +120,7 @@ static ScoreProblem make_problem(const void* q, int64_t q_sb, int64_t q_sh, int6
   p.k = k; p.v = v; p.kv_sh = (int64_t)Lk * D; p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.Lk = Lk; p.D = D;
   p.W = window; p.g = Hq / Hkv; p.M = p.g * window;
   p.scale = (float)(1.0 / std::sqrt((double)D));
-  p.eps = eps; p.round_mode = round_p; p.scores = scores;
+  p.eps = eps; p.round_mode = round_p; p.scores = scores; p.status = nullptr;
   return p;
 }
 
@@ -449,4 +449,107 @@ int dropkv_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q
                                  out, workspace, reinterpret_cast<cudaStream_t>(stream));
 }
 
+// ---------------------------------------------------------------------------
+// Ragged batch: one call, keep_len per sequence on the device
+// ---------------------------------------------------------------------------
+// Workspace: [256 B: OR of the scorers' status words][scorer scratch, the largest
+// any sequence needs (the scorer launches run one after another on the stream)]
+// [each sequence's score rows, 256-byte aligned].
+static size_t varlen_layout(int n_seq, const dropkv_varlen_seq* seqs, int Hq, int Hkv, int D, int window,
+                            size_t* off_scores, int64_t* score_off /* [n_seq] floats, may be NULL */) {
+  size_t scratch = 0;
+  for (int i = 0; i < n_seq; ++i) {
+    const int W = std::min(window, seqs[i].Lq);
+    scratch = std::max(scratch, dropkv_scores_workspace_size(seqs[i].B, Hq, Hkv, seqs[i].Lk, D, W));
+  }
+  const size_t off = align_up(256 + scratch, 256);
+  size_t bytes = off;
+  for (int i = 0; i < n_seq; ++i) {
+    if (score_off) score_off[i] = (int64_t)((bytes - off) / 4);
+    bytes = align_up(bytes + (size_t)seqs[i].B * Hkv * seqs[i].Lk * 4, 256);
+  }
+  if (off_scores) *off_scores = off;
+  return bytes;
+}
+
+size_t dropkv_compress_varlen_workspace_size(int n_seq, const dropkv_varlen_seq* seqs, int Hq, int Hkv, int D,
+                                             int window) {
+  if (n_seq < 1 || n_seq > DROPKV_VARLEN_MAX_SEQS || !seqs || Hq < 1 || Hkv < 1 || D < 1 || window < 1) return 0;
+  for (int i = 0; i < n_seq; ++i)
+    if (seqs[i].B < 1 || seqs[i].Lk < 1 || seqs[i].Lq < 1) return 0;
+  return varlen_layout(n_seq, seqs, Hq, Hkv, D, window, nullptr, nullptr);
+}
+
+int dropkv_compress_varlen(int n_seq, const dropkv_varlen_seq* seqs, int dtype, int Hq, int Hkv, int D, int window,
+                           float eps, int round_p, int kernel_size, int protect_window, double keep_ratio,
+                           int keep_window, const int64_t* total_tokens, const int64_t* max_keep_len,
+                           int32_t* keep_len_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (n_seq < 1 || n_seq > DROPKV_VARLEN_MAX_SEQS)
+    return fail(DROPKV_ERR_ARG, "n_seq must be in [1, %d], got %d", DROPKV_VARLEN_MAX_SEQS, n_seq);
+  if (!seqs || !keep_len_out) return fail(DROPKV_ERR_ARG, "seqs and keep_len_out must be non-NULL");
+  if (!(keep_ratio > 0.0 && keep_ratio <= 1.0))
+    return fail(DROPKV_ERR_ARG, "keep_ratio must be in (0, 1], got %g", keep_ratio);
+  if (keep_window < 0) return fail(DROPKV_ERR_ARG, "keep_window must be >= 0, got %d", keep_window);
+  if (window < 1) return fail(DROPKV_ERR_ARG, "window_size must be a positive int, got %d", window);
+  int64_t rows = 0;
+  for (int i = 0; i < n_seq; ++i) {
+    const dropkv_varlen_seq& q = seqs[i];
+    const int W = std::min(window, q.Lq);
+    int rc = check_score_args(q.q, q.Lq, q.k, q.v, dtype, q.B, Hq, Hkv, q.Lk, D, W, round_p);
+    if (!rc) rc = check_select_args(q.B, Hkv, q.Lk, kernel_size, protect_window, 1);
+    if (rc) return fail(rc, "sequence %d: %s", i, dropkv_last_error());
+    if (q.cap < 1 || q.cap > q.Lk) return fail(DROPKV_ERR_ARG, "sequence %d: cap must be in [1, Lk=%d], got %d", i, q.Lk, q.cap);
+    if (!q.keep_idx || !q.k_out || !q.v_out)
+      return fail(DROPKV_ERR_ARG, "sequence %d: keep_idx, k_out and v_out must be non-NULL", i);
+    if (!select_gather_supported(q.Lk, kernel_size))
+      return fail(DROPKV_ERR_UNSUPPORTED, "sequence %d: %d keys exceed the one-launch selection", i, q.Lk);
+    rows += (int64_t)q.B * Hkv;
+  }
+  if (rows > 65535) return fail(DROPKV_ERR_ARG, "the batch has %lld (b, KV head) rows; at most 65535", (long long)rows);
+  VarlenTable t;
+  std::memset(&t, 0, sizeof(t));
+  size_t off_scores;
+  int64_t score_off[DROPKV_VARLEN_MAX_SEQS];
+  const size_t need = varlen_layout(n_seq, seqs, Hq, Hkv, D, window, &off_scores, score_off);
+  int rc = check_ws(workspace, workspace_bytes, need);
+  if (rc) return rc;
+  char* base = reinterpret_cast<char*>(workspace);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int* status = reinterpret_cast<int*>(base);
+  cudaError_t e = cudaMemsetAsync(status, 0, 4, st);
+  if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "status reset: %s", cudaGetErrorString(e));
+  t.n = n_seq;
+  t.protect = protect_window;
+  t.keep_window = keep_window;
+  t.keep_ratio = keep_ratio;
+  t.total_tokens = total_tokens;
+  t.max_keep_len = max_keep_len;
+  t.keep_len_out = keep_len_out;
+  t.scores = reinterpret_cast<const float*>(base + off_scores);
+  int row0 = 0;
+  for (int i = 0; i < n_seq; ++i) {
+    const dropkv_varlen_seq& q = seqs[i];
+    float* sc = reinterpret_cast<float*>(base + off_scores) + score_off[i];
+    ScoreProblem p = make_problem(q.q, q.q_sb, q.q_sh, q.q_ss, q.q_sd, q.Lq, q.k, q.v, q.B, Hq, Hkv, q.Lk, D,
+                                  std::min(window, q.Lq), eps, round_p, sc);
+    p.status = status;
+    if ((rc = run_scores(p, dtype, base + 256, st))) return rc;
+    VarlenSeq& v = t.s[i];
+    v.k = q.k;
+    v.v = q.v;
+    v.keep_idx = q.keep_idx;
+    v.k_out = q.k_out;
+    v.v_out = q.v_out;
+    v.score_off = score_off[i];
+    v.row0 = row0;
+    v.rows = q.B * Hkv;
+    v.lk = q.Lk;
+    v.cap = q.cap;
+    row0 += v.rows;
+  }
+  t.rows = row0;
+  return launch_select_gather_varlen(t, kernel_size, elem_bytes_of(dtype), D, st);
+}
+
 }  // extern "C"
+

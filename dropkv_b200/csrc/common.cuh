@@ -80,6 +80,7 @@ struct ScoreProblem {
   float eps;
   int round_mode;
   float* scores;  // [B*Hkv, Lk]
+  int* status;    // where the tensor-core scorer ORs its status bits (nullptr: its own workspace word)
 };
 
 // Scratch layout of the split-K scorer (fp32 regions, 256-byte aligned).
@@ -97,6 +98,60 @@ int num_sms_current_device();
 ScorePlan plan_scores(int B, int Hkv, int Lk, int M, int D);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// A ragged batch for one call (dropkv_compress_varlen): up to kVarlenMaxSeqs
+// sequences, each with its own key count and batch of (b, KV head) rows, passed to
+// the selection and gather kernels by value as a kernel parameter.
+constexpr int kVarlenMaxSeqs = 32;
+
+struct VarlenSeq {
+  const void* k;        // [B, Hkv, lk, D] contiguous
+  const void* v;
+  int64_t* keep_idx;    // [B, Hkv, cap]
+  void* k_out;          // [B, Hkv, cap, D]
+  void* v_out;
+  int64_t score_off;    // floats before the sequence's first score row in the packed buffer
+  int row0;             // its first row in the batch
+  int rows;             // B * Hkv
+  int lk;
+  int cap;              // rows of room per (b, KV head) in keep_idx / k_out / v_out
+};
+
+struct VarlenTable {
+  int n;                        // sequences
+  int rows;                     // rows of the whole batch
+  int protect;                  // protect window (clamped to each sequence's lk)
+  int keep_window;              // window_size of the keep_len rule
+  double keep_ratio;
+  const int64_t* total_tokens;  // [n] on the device, or NULL (base = lk)
+  const int64_t* max_keep_len;  // [n] on the device, or NULL; entries < 0 set no cap
+  int32_t* keep_len_out;        // [n] on the device
+  const float* scores;          // packed score rows of all sequences
+  VarlenSeq s[kVarlenMaxSeqs];
+};
+
+// Sequence of batch row `row` (rows are grouped by sequence, in order).
+__device__ __forceinline__ int varlen_seq_of(const VarlenTable& t, int row) {
+  int s = 0;
+  while (s + 1 < t.n && row >= t.s[s + 1].row0) ++s;
+  return s;
+}
+
+// keep_len = min(lk, max(int(keep_ratio * base), keep_window, 1)), base =
+// total_tokens or lk, then min(max_keep_len) (dropkv_cache.py:470-473; Python's
+// int() of a double product truncates toward zero, as the conversion here does),
+// and at most the sequence's output room.
+__device__ __forceinline__ int varlen_keep_len(const VarlenTable& t, int s) {
+  const int lk = t.s[s].lk;
+  const double base = t.total_tokens ? (double)t.total_tokens[s] : (double)lk;
+  const double prod = t.keep_ratio * base;
+  long long kl = prod >= (double)lk ? (long long)lk : (long long)prod;
+  kl = kl < t.keep_window ? t.keep_window : kl;
+  kl = kl < 1 ? 1 : kl;
+  kl = kl > lk ? lk : kl;
+  if (t.max_keep_len && t.max_keep_len[s] >= 0 && t.max_keep_len[s] < kl) kl = t.max_keep_len[s];
+  return (int)(kl > t.s[s].cap ? t.s[s].cap : kl);
+}
 
 // One bit per device (index < 64) recording that a per-device set-up step (kernel
 // attributes) has run.  Several host threads may call into the library at once:
@@ -143,5 +198,8 @@ int launch_select_gather(const float* scores, int BH, int Lk, int kernel_size, i
 int launch_gather(const void* k, const void* v, int elem_bytes, int BH, int Lk, int D,
                   const int64_t* keep_idx, int keep_len, void* k_out, void* v_out,
                   cudaStream_t st, int64_t in_sh = 0, int64_t out_sh = 0);
+// A ragged batch: one selection launch and one gather launch over every row of
+// the table (t.scores filled); the longest row must pass select_gather_supported.
+int launch_select_gather_varlen(const VarlenTable& t, int kernel_size, int elem_bytes, int D, cudaStream_t st);
 
 }  // namespace dropkv

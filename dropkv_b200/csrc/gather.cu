@@ -15,22 +15,15 @@ namespace {
 constexpr int GT_NT = 256;  // threads per block
 constexpr int GT_U = 2;     // chunks per thread and step: 2 K and 2 V loads in flight
 
-// in_sh / out_sh: vectors between consecutive heads of the input and the output.
-// Block x of row bh handles steps x, x + gridDim.x, ...; a step is GT_U * GT_NT
-// consecutive chunks, and all its index and data loads are issued before its stores.
+// One row: ko[i, :] = kb[ib[i], :] and vo[i, :] = vb[ib[i], :] for i < keep_len, rows
+// of CR vectors. Block x of the row handles steps x, x + gridDim.x, ...; a step is
+// GT_U * GT_NT consecutive chunks, and all its index and data loads are issued
+// before its stores.
 template <typename VT>
-__global__ void __launch_bounds__(GT_NT) gather_kernel(const VT* __restrict__ k, const VT* __restrict__ v,
-                                                       const int64_t* __restrict__ idx, int Lk, int keep_len,
-                                                       int CR, VT* __restrict__ ko, VT* __restrict__ vo,
-                                                       int64_t in_sh, int64_t out_sh) {
-  const int bh = blockIdx.y;
+__device__ __forceinline__ void gather_row(const VT* __restrict__ kb, const VT* __restrict__ vb,
+                                           const int64_t* __restrict__ ib, int Lk, int keep_len, int CR,
+                                           VT* __restrict__ kob, VT* __restrict__ vob) {
   const int64_t n = (int64_t)keep_len * CR;
-  const int64_t* ib = idx + (size_t)bh * keep_len;
-  const VT* kb = k + (size_t)bh * in_sh;
-  const VT* vb = v + (size_t)bh * in_sh;
-  VT* kob = ko + (size_t)bh * out_sh;
-  VT* vob = vo + (size_t)bh * out_sh;
-  pdl_wait();  // keep_idx may come from the kernel before this one
   for (int64_t c0 = (int64_t)blockIdx.x * (GT_U * GT_NT) + threadIdx.x; c0 < n;
        c0 += (int64_t)gridDim.x * (GT_U * GT_NT)) {
     int64_t src[GT_U], i[GT_U];
@@ -61,6 +54,34 @@ __global__ void __launch_bounds__(GT_NT) gather_kernel(const VT* __restrict__ k,
       }
     }
   }
+}
+
+// in_sh / out_sh: vectors between consecutive heads of the input and the output.
+template <typename VT>
+__global__ void __launch_bounds__(GT_NT) gather_kernel(const VT* __restrict__ k, const VT* __restrict__ v,
+                                                       const int64_t* __restrict__ idx, int Lk, int keep_len,
+                                                       int CR, VT* __restrict__ ko, VT* __restrict__ vo,
+                                                       int64_t in_sh, int64_t out_sh) {
+  const int bh = blockIdx.y;
+  pdl_wait();  // keep_idx may come from the kernel before this one
+  gather_row<VT>(k + (size_t)bh * in_sh, v + (size_t)bh * in_sh, idx + (size_t)bh * keep_len, Lk, keep_len, CR,
+                 ko + (size_t)bh * out_sh, vo + (size_t)bh * out_sh);
+}
+
+// A ragged batch: row blockIdx.y of the table's batch, with its sequence's
+// lengths; keep_len is the one the selection wrote to t.keep_len_out.
+template <typename VT>
+__global__ void __launch_bounds__(GT_NT) gather_varlen_kernel(const __grid_constant__ VarlenTable t, int CR) {
+  const int row = blockIdx.y;
+  const int s = varlen_seq_of(t, row);
+  const VarlenSeq& q = t.s[s];
+  const int b = row - q.row0;
+  pdl_wait();  // keep_idx and keep_len_out come from the selection
+  const int keep_len = t.keep_len_out[s];
+  const int64_t in_sh = (int64_t)q.lk * CR, out_sh = (int64_t)q.cap * CR;
+  gather_row<VT>(reinterpret_cast<const VT*>(q.k) + b * in_sh, reinterpret_cast<const VT*>(q.v) + b * in_sh,
+                 q.keep_idx + (size_t)b * q.cap, q.lk, keep_len, CR, reinterpret_cast<VT*>(q.k_out) + b * out_sh,
+                 reinterpret_cast<VT*>(q.v_out) + b * out_sh);
 }
 
 template <typename VT>
@@ -96,6 +117,33 @@ int launch_vec(const void* k, const void* v, int BH, int Lk, int row_bytes, cons
 
 bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+template <typename VT>
+int launch_varlen_vec(const VarlenTable& t, int row_bytes, cudaStream_t st) {
+  const int CR = row_bytes / (int)sizeof(VT);
+  int cap_max = 1;
+  for (int i = 0; i < t.n; ++i) cap_max = std::max(cap_max, t.s[i].cap);
+  const int64_t n = (int64_t)cap_max * CR;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t steps = (n + GT_U * GT_NT - 1) / (GT_U * GT_NT);
+  const int64_t target = std::max<int64_t>(1, (int64_t)sms * (2048 / GT_NT) / t.rows);
+  const int64_t per_block = (steps + target - 1) / target;
+  int bx = (int)std::min<int64_t>((steps + per_block - 1) / per_block, 65535);
+  if (bx < 1) bx = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(bx, t.rows);
+  cfg.blockDim = dim3(GT_NT);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gather_varlen_kernel<VT>, t, CR);
+  if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "varlen gather launch: %s", cudaGetErrorString(e));
+  return check_launch("gather_varlen");
+}
+
 }  // namespace
 
 int launch_gather(const void* k, const void* v, int elem_bytes, int BH, int Lk, int D,
@@ -117,6 +165,27 @@ int launch_gather(const void* k, const void* v, int elem_bytes, int BH, int Lk, 
     }
   }
   return fail(DROPKV_ERR_ARG, "gather: K/V and outputs must be at least 2-byte aligned");
+}
+
+// Vector width: the widest that every sequence's rows, pointers and row strides allow.
+int launch_gather_varlen(const VarlenTable& t, int elem_bytes, int D, cudaStream_t st) {
+  if (t.rows < 1) return DROPKV_OK;
+  const int row_bytes = D * elem_bytes;
+  for (int w : {16, 8, 4, 2}) {
+    bool ok = row_bytes % w == 0;
+    for (int i = 0; i < t.n && ok; ++i) {
+      const VarlenSeq& q = t.s[i];
+      ok = aligned(q.k, w) && aligned(q.v, w) && aligned(q.k_out, w) && aligned(q.v_out, w);
+    }
+    if (!ok) continue;
+    switch (w) {
+      case 16: return launch_varlen_vec<uint4>(t, row_bytes, st);
+      case 8: return launch_varlen_vec<uint2>(t, row_bytes, st);
+      case 4: return launch_varlen_vec<uint32_t>(t, row_bytes, st);
+      case 2: return launch_varlen_vec<uint16_t>(t, row_bytes, st);
+    }
+  }
+  return fail(DROPKV_ERR_ARG, "varlen gather: K/V and outputs must be at least 2-byte aligned");
 }
 
 }  // namespace dropkv

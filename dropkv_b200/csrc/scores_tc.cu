@@ -1189,7 +1189,7 @@ static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cuda
   a.pscale = bf16 ? 1.0f : 32768.0f;
   a.q_tma = q_tma ? 1 : 0;
   a.ctr = reinterpret_cast<int*>(base + t.off_ctr);
-  a.status = reinterpret_cast<int*>(base + t.off_status);
+  a.status = p.status ? p.status : reinterpret_cast<int*>(base + t.off_status);
   a.trace = reinterpret_cast<unsigned long long*>(base + t.off_trace);
   a.part_m = reinterpret_cast<float*>(base + t.off_pm);
   a.part_s = reinterpret_cast<float*>(base + t.off_ps);

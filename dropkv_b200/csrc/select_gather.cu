@@ -106,15 +106,17 @@ __device__ __forceinline__ void sg_cluster_wait() {
 
 // RT: the pooling radius when known at compile time (pooling in registers), or -1.
 // KPT: positions per thread (8, 16 or 32).
+// One row (srow: its Lk scores) of the selection, run by the calling CTA's whole
+// cluster; the kept positions go to orow[0 .. keep_len). `waited`: the caller has
+// already waited for the kernel before this one.
 template <int RT, int KPT>
-__global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* __restrict__ scores, int Lk,
-                                                                  int chunk, int radius_rt, int protect,
-                                                                  int keep_len, int64_t* __restrict__ keep_idx) {
+__device__ __forceinline__ void sg_select_row(const float* __restrict__ srow, int Lk, int chunk, int radius_rt,
+                                              int protect, int keep_len, int64_t* __restrict__ orow0,
+                                              bool waited) {
   const int radius = RT >= 0 ? RT : radius_rt;
   cg::cluster_group cluster = cg::this_cluster();
   const int CL = (int)cluster.num_blocks();
   const int r = (int)cluster.block_rank();
-  const int row = blockIdx.x / CL;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __shared__ SgShared S;
   extern __shared__ uint32_t dyn[];
@@ -128,9 +130,8 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
 
   const int j0 = min(Lk, r * chunk), j1 = min(Lk, j0 + chunk);
   const int n = j1 - j0;
-  pdl_wait();               // the scores come from the kernel before this one
+  if (!waited) pdl_wait();  // the scores come from the kernel before this one
   pdl_launch_dependents();  // the gather may be scheduled on the SMs left free
-  const float* srow = scores + (size_t)row * Lk;
   const int pstart = Lk - protect;
 
   // ---- 1. sliding max --------------------------------------------------------
@@ -386,7 +387,7 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
   __syncthreads();
   const int out_before = S.before[0], eq_before = S.before[1];
   const int need_local = max(0, need_eq - eq_before);  // ties this CTA keeps, lowest index first
-  int64_t* orow = keep_idx + (size_t)row * keep_len + out_before;
+  int64_t* orow = orow0 + out_before;
   int g = cpre & 0xffff, e = cpre >> 16;
   const int jx = j0 + x0;
 #pragma unroll
@@ -402,6 +403,36 @@ __global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* _
     }
   }
   cluster.sync();  // keep this CTA's shared memory alive until the cluster has read it
+}
+
+// Rows of one length: row blockIdx.x / CL of scores [rows, Lk] into keep_idx [rows, keep_len].
+template <int RT, int KPT>
+__global__ void __launch_bounds__(SG_NT, 1) cluster_select_kernel(const float* __restrict__ scores, int Lk,
+                                                                  int chunk, int radius_rt, int protect,
+                                                                  int keep_len, int64_t* __restrict__ keep_idx) {
+  const int row = blockIdx.x / (int)cg::this_cluster().num_blocks();
+  sg_select_row<RT, KPT>(scores + (size_t)row * Lk, Lk, chunk, radius_rt, protect, keep_len,
+                         keep_idx + (size_t)row * keep_len, false);
+}
+
+// A ragged batch: row blockIdx.x / CL of the batch belongs to the sequence the table
+// names; its length, chunk and keep_len (the keep_len rule, evaluated here) are the
+// sequence's own. The dynamic shared memory is sized for the longest row.
+template <int RT, int KPT>
+__global__ void __launch_bounds__(SG_NT, KPT <= 16 ? 2 : 1) cluster_select_varlen_kernel(const __grid_constant__ VarlenTable t,
+                                                                         int radius_rt) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int CL = (int)cluster.num_blocks();
+  const int row = blockIdx.x / CL;
+  const int s = varlen_seq_of(t, row);
+  const VarlenSeq& q = t.s[s];
+  pdl_wait();  // the scores (and possibly total_tokens / max_keep_len) come from earlier kernels
+  const int keep_len = varlen_keep_len(t, s);
+  if (row == q.row0 && cluster.block_rank() == 0 && threadIdx.x == 0) t.keep_len_out[s] = keep_len;
+  if (keep_len == 0) return;  // the whole cluster returns here, before any cluster barrier
+  const int lk = q.lk, b = row - q.row0;
+  sg_select_row<RT, KPT>(t.scores + q.score_off + (size_t)b * lk, lk, (lk + CL - 1) / CL, radius_rt,
+                         min(t.protect, lk), keep_len, q.keep_idx + (size_t)b * q.cap, true);
 }
 
 }  // namespace
@@ -434,32 +465,53 @@ bool select_gather_supported(int Lk, int kernel_size) {
 }
 
 using SgKernel = void (*)(const float*, int, int, int, int, int, int64_t*);
+using SgKernelV = void (*)(VarlenTable, int);
 constexpr int SG_VARIANTS = 6;
 
 // kernel for the radius (5: the default kernel_size 11) and positions per thread
+static int sg_variant(bool r5, int kpt) { return (r5 ? 3 : 0) + (kpt == 8 ? 0 : (kpt == 16 ? 1 : 2)); }
+
 static SgKernel sg_kernel(bool r5, int kpt, int* variant) {
   static const SgKernel table[SG_VARIANTS] = {
       cluster_select_kernel<-1, 8>, cluster_select_kernel<-1, 16>, cluster_select_kernel<-1, 32>,
       cluster_select_kernel<5, 8>,  cluster_select_kernel<5, 16>,  cluster_select_kernel<5, 32>};
-  *variant = (r5 ? 3 : 0) + (kpt == 8 ? 0 : (kpt == 16 ? 1 : 2));
+  *variant = sg_variant(r5, kpt);
   return table[*variant];
 }
 
-// Function attributes, set once per device and variant: the largest dynamic
+static SgKernelV sg_kernel_varlen(int variant) {
+  static const SgKernelV table[SG_VARIANTS] = {
+      cluster_select_varlen_kernel<-1, 8>, cluster_select_varlen_kernel<-1, 16>,
+      cluster_select_varlen_kernel<-1, 32>, cluster_select_varlen_kernel<5, 8>,
+      cluster_select_varlen_kernel<5, 16>, cluster_select_varlen_kernel<5, 32>};
+  return table[variant];
+}
+
+// Function attributes, set once per device and kernel: the largest dynamic
 // shared memory any chunk can ask for, and 16-CTA clusters.
-static int sg_prepare(SgKernel kern, int variant, size_t smem) {
-  static DeviceOnce done[SG_VARIANTS];
+template <typename K>
+static int sg_prepare_kernel(K kern, DeviceOnce& done, size_t smem) {
   const int max_dyn = 227 * 1024 - (int)sizeof(SgShared);
   if (smem > (size_t)max_dyn) return fail(DROPKV_ERR_UNSUPPORTED, "cluster select needs %zu bytes", smem);
   int dev = 0;
   cudaGetDevice(&dev);
-  if (done[variant].done(dev)) return DROPKV_OK;
+  if (done.done(dev)) return DROPKV_OK;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn) != cudaSuccess)
     return fail(DROPKV_ERR_CUDA, "cannot set shared memory size %d for the cluster select", max_dyn);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
     return fail(DROPKV_ERR_CUDA, "cannot allow 16-CTA clusters for the cluster select");
-  done[variant].mark(dev);
+  done.mark(dev);
   return DROPKV_OK;
+}
+
+static int sg_prepare(SgKernel kern, int variant, size_t smem) {
+  static DeviceOnce done[SG_VARIANTS];
+  return sg_prepare_kernel(kern, done[variant], smem);
+}
+
+static int sg_prepare_varlen(int variant, size_t smem) {
+  static DeviceOnce done[SG_VARIANTS];
+  return sg_prepare_kernel(sg_kernel_varlen(variant), done[variant], smem);
 }
 
 // Clusters of `cl` CTAs that can be resident at once on this device (a cluster
@@ -499,8 +551,13 @@ static int sg_active_clusters(SgKernel kern, int variant, int cl, size_t smem) {
   return n;
 }
 
-static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
-                                 int64_t* keep_idx, cudaStream_t st) {
+struct SgChoice {
+  int cl, chunk, variant;
+  size_t smem;
+};
+
+// Cluster size, chunk and kernel variant for BH rows of (at most) Lk positions.
+static int plan_cluster_select(int BH, int Lk, int kernel_size, SgChoice* out) {
   const int radius = kernel_size / 2;
   const bool r5 = radius == 5;
   int chunk;
@@ -536,27 +593,48 @@ static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel
       cl = c;
       chunk = ch;
       smem = sm;
-      kern = kr;
+      variant = var;
     }
     waves = w;
   }
+  out->cl = cl;
+  out->chunk = chunk;
+  out->variant = variant;
+  out->smem = smem;
+  return DROPKV_OK;
+}
+
+// cluster launch of `rows` rows of `cl` CTAs, allowed to start while the kernel
+// before it finishes (programmatic dependent launch)
+template <typename K, typename... Args>
+static int sg_launch(K kern, int rows, const SgChoice& c, cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(BH * cl);
+  cfg.gridDim = dim3(rows * c.cl);
   cfg.blockDim = dim3(SG_NT);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = c.smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cl;
+  attr[0].val.clusterDim.x = c.cl;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, scores, Lk, chunk, radius, protect, keep_len, keep_idx);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
   if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "cluster select launch: %s", cudaGetErrorString(e));
   return check_launch("cluster_select");
+}
+
+static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
+                                 int64_t* keep_idx, cudaStream_t st) {
+  SgChoice c;
+  int rc = plan_cluster_select(BH, Lk, kernel_size, &c);
+  if (rc) return rc;
+  int variant;
+  SgKernel kern = sg_kernel(kernel_size / 2 == 5, sg_kpt(c.chunk), &variant);
+  return sg_launch(kern, BH, c, st, scores, Lk, c.chunk, kernel_size / 2, protect, keep_len, keep_idx);
 }
 
 // Selection into keep_idx and, when K/V are given, the gather of the kept rows.
@@ -566,6 +644,22 @@ int launch_select_gather(const float* scores, int BH, int Lk, int kernel_size, i
   int rc = launch_cluster_select(scores, BH, Lk, kernel_size, protect, keep_len, keep_idx, st);
   if (rc || k == nullptr) return rc;
   return launch_gather(k, v, elem_bytes, BH, Lk, D, keep_idx, keep_len, ko, vo, st, in_sh, out_sh);
+}
+
+int launch_gather_varlen(const VarlenTable& t, int elem_bytes, int D, cudaStream_t st);
+
+// A ragged batch: the plan of the longest row serves every row (a shorter row's
+// chunk is smaller, so the same shared memory holds it).
+int launch_select_gather_varlen(const VarlenTable& t, int kernel_size, int elem_bytes, int D, cudaStream_t st) {
+  if (t.rows < 1) return DROPKV_OK;
+  int lk_max = 1;
+  for (int i = 0; i < t.n; ++i) lk_max = std::max(lk_max, t.s[i].lk);
+  SgChoice c;
+  int rc = plan_cluster_select(t.rows, lk_max, kernel_size, &c);
+  if (rc) return rc;
+  if ((rc = sg_prepare_varlen(c.variant, c.smem))) return rc;
+  if ((rc = sg_launch(sg_kernel_varlen(c.variant), t.rows, c, st, t, kernel_size / 2))) return rc;
+  return launch_gather_varlen(t, elem_bytes, D, st);
 }
 
 }  // namespace dropkv

@@ -11,6 +11,10 @@
 * ``compress``           -- the whole path in one C call.
 * ``compress_strided``   -- the same over preallocated row buffers (in-place
   chunked prefill storage, no concatenation).
+* ``compress_varlen`` / ``VarlenCompressor`` -- a ragged batch (sequences of
+  different lengths) in one C call, keep_len per sequence evaluated on the device
+  from the reference's rule (dropkv_cache.py:470-473) with per-sequence
+  total_tokens / max_keep_len (the chunked-prefill policies, dropkv_cache.py:749-788).
 """
 
 from __future__ import annotations
@@ -463,3 +467,141 @@ class HostPipeline:
             last = torch.cuda.Event()
             last.record(self.d2h)
         return last
+
+
+def _device_i64(x, n: int, device, what: str):
+    """None, a device int64 tensor [n], or a sequence of n ints (None -> -1)."""
+    if x is None:
+        return None
+    if isinstance(x, torch.Tensor):
+        if x.dtype != torch.int64 or x.numel() != n or not x.is_cuda:
+            raise ValueError(f"{what} must be an int64 CUDA tensor of {n} entries")
+        return x.contiguous()
+    vals = [-1 if v is None else int(v) for v in x]
+    if len(vals) != n:
+        raise ValueError(f"{what} needs {n} entries, got {len(vals)}")
+    return torch.tensor(vals, dtype=torch.int64, device=device)
+
+
+class VarlenCompressor:
+    """Pre-planned ``dropkv_compress_varlen`` for a fixed ragged batch.
+
+    ``shapes``: per sequence (B, Lq, Lk) -- B rows of the sequence's batch (its
+    layers stacked, say), Lq query rows, Lk keys -- at most ``VARLEN_MAX_SEQS``
+    sequences. Holds per sequence the outputs keep_idx [B, Hkv, cap] and
+    K_c / V_c [B, Hkv, cap, D] (``cap``: rows of room, default Lk), the device
+    vector ``keep_len`` [n] (int32) and the workspace, so ``run`` issues exactly one
+    C-ABI call and allocates nothing (CUDA-graph capturable). Rows of an output
+    past its sequence's keep_len are left as they were.
+    """
+
+    def __init__(self, shapes, Hq: int, Hkv: int, D: int, dtype: torch.dtype, window: int, kernel_size: int,
+                 keep_ratio: float, caps=None, keep_window: int | None = None, protect_window: int | None = None,
+                 eps: float = 1e-6, round_p: bool = True, device="cuda"):
+        n = len(shapes)
+        if not 1 <= n <= _lib.VARLEN_MAX_SEQS:
+            raise ValueError(f"1..{_lib.VARLEN_MAX_SEQS} sequences per VarlenCompressor, got {n}")
+        if dtype not in _DTYPE_CODE:
+            raise TypeError(f"unsupported dtype {dtype}")
+        self.shapes = [tuple(int(x) for x in sh) for sh in shapes]
+        self.caps = [lk for (_, _, lk) in self.shapes] if caps is None else [int(c) for c in caps]
+        if len(self.caps) != n:
+            raise ValueError(f"caps needs {n} entries")
+        self.Hq, self.Hkv, self.D, self.dtype = int(Hq), int(Hkv), int(D), dtype
+        self.window, self.kernel_size = int(window), int(kernel_size)
+        self.keep_ratio = float(keep_ratio)
+        self.keep_window = int(window if keep_window is None else keep_window)
+        self.protect = int(window if protect_window is None else protect_window)
+        self.eps = float(eps)
+        self.round = _ROUND_CODE[dtype] if round_p else _lib.ROUND_NONE
+        self.device = torch.device(device)
+        lib = _lib.load()
+        self._seqs = (_lib.VarlenSeq * n)()
+        with torch.cuda.device(self.device):
+            self.outputs = []
+            for i, ((B, Lq, Lk), cap) in enumerate(zip(self.shapes, self.caps)):
+                idx = torch.empty(B, Hkv, cap, dtype=torch.int64, device=self.device)
+                kc = torch.empty(B, Hkv, cap, D, dtype=dtype, device=self.device)
+                vc = torch.empty_like(kc)
+                self.outputs.append((idx, kc, vc))
+                sq = self._seqs[i]
+                sq.Lq, sq.B, sq.Lk, sq.cap = Lq, B, Lk, cap
+                sq.keep_idx, sq.k_out, sq.v_out = idx.data_ptr(), kc.data_ptr(), vc.data_ptr()
+            self.keep_len = torch.zeros(n, dtype=torch.int32, device=self.device)
+            nbytes = lib.dropkv_compress_varlen_workspace_size(n, self._seqs, self.Hq, self.Hkv, self.D, self.window)
+            if nbytes == 0:
+                raise ValueError("invalid ragged batch shapes")
+            self.workspace = _workspace(nbytes, self.device)
+
+    def run(self, Qs, Ks, Vs, total_tokens=None, max_keep_len=None, stream: int | None = None):
+        """Compress sequence i from Qs[i] [B, Hq, Lq, D] (any strides) and Ks[i], Vs[i]
+        [B, Hkv, Lk, D] (contiguous). ``total_tokens`` / ``max_keep_len``: None, an
+        int64 CUDA tensor [n] or n ints (a None / negative max_keep_len entry sets no
+        cap). Returns (keep_len [n] int32 on the device, outputs)."""
+        n = len(self.shapes)
+        if not (len(Qs) == len(Ks) == len(Vs) == n):
+            raise ValueError(f"expected {n} sequences")
+        _require_cuda(*Qs, *Ks, *Vs)
+        for i, (Q, K, V) in enumerate(zip(Qs, Ks, Vs)):
+            B, Lq, Lk = self.shapes[i]
+            if tuple(Q.shape) != (B, self.Hq, Lq, self.D) or tuple(K.shape) != (B, self.Hkv, Lk, self.D) \
+                    or K.shape != V.shape:
+                raise ValueError(f"sequence {i}: shapes do not match this VarlenCompressor")
+            if Q.dtype != self.dtype or K.dtype != self.dtype or V.dtype != self.dtype:
+                raise TypeError(f"sequence {i}: expected {self.dtype}")
+            if not (K.is_contiguous() and V.is_contiguous()):
+                raise ValueError(f"sequence {i}: K and V must be contiguous")
+            sq = self._seqs[i]
+            sq.q = Q.data_ptr()
+            sq.q_sb, sq.q_sh, sq.q_ss, sq.q_sd = Q.stride()
+            sq.k, sq.v = K.data_ptr(), V.data_ptr()
+        tt = _device_i64(total_tokens, n, self.device, "total_tokens")
+        mk = _device_i64(max_keep_len, n, self.device, "max_keep_len")
+        lib = _lib.load()
+        st = _stream(self.device) if stream is None else stream
+        rc = lib.dropkv_compress_varlen(n, self._seqs, _DTYPE_CODE[self.dtype], self.Hq, self.Hkv, self.D,
+                                        self.window, self.eps, self.round, self.kernel_size, self.protect,
+                                        self.keep_ratio, self.keep_window,
+                                        tt.data_ptr() if tt is not None else None,
+                                        mk.data_ptr() if mk is not None else None,
+                                        self.keep_len.data_ptr(), self.workspace.data_ptr(),
+                                        self.workspace.numel(), st)
+        _lib.check(rc, "dropkv_compress_varlen")
+        if _CHECK_STATUS and not torch.cuda.is_current_stream_capturing():
+            s = int(self.workspace[:4].view(torch.int32).item())
+            if s != 0:
+                raise _lib.DropKVError(_lib.ERR_DEVICE, f"dropkv_compress_varlen: device status {s} "
+                                                        "(a bounded wait timed out)")
+        return self.keep_len, self.outputs
+
+
+def compress_varlen(Qs, Ks, Vs, window: int, kernel_size: int, keep_ratio: float, total_tokens=None,
+                    max_keep_len=None, caps=None, keep_window: int | None = None,
+                    protect_window: int | None = None, eps: float = 1e-6, round_p: bool = True):
+    """A ragged batch of sequences (lists Qs, Ks, Vs: [B_i, Hq, Lq_i, D] and
+    [B_i, Hkv, Lk_i, D]) compressed with one C call per ``VARLEN_MAX_SEQS``
+    sequences; keep_len per sequence is evaluated on the device. Returns
+    (keep_len [n] int32 on the device, [(keep_idx, K_c, V_c)] with cap rows each,
+    the rows past keep_len unspecified)."""
+    n = len(Qs)
+    if n == 0:
+        raise ValueError("empty batch")
+    _, Hq, _, D = Qs[0].shape
+    Hkv = Ks[0].shape[1]
+    dev = Qs[0].device
+    tt = _device_i64(total_tokens, n, dev, "total_tokens")
+    mk = _device_i64(max_keep_len, n, dev, "max_keep_len")
+    lens, outs = [], []
+    step = _lib.VARLEN_MAX_SEQS
+    for a in range(0, n, step):
+        b = min(n, a + step)
+        shapes = [(Q.shape[0], Q.shape[2], K.shape[2]) for Q, K in zip(Qs[a:b], Ks[a:b])]
+        comp = VarlenCompressor(shapes, Hq, Hkv, D, Qs[0].dtype, window, kernel_size, keep_ratio,
+                                caps=None if caps is None else caps[a:b], keep_window=keep_window,
+                                protect_window=protect_window, eps=eps, round_p=round_p, device=dev)
+        kl, o = comp.run([Q for Q in Qs[a:b]], [K.contiguous() for K in Ks[a:b]], [V.contiguous() for V in Vs[a:b]],
+                         total_tokens=None if tt is None else tt[a:b],
+                         max_keep_len=None if mk is None else mk[a:b])
+        lens.append(kl)
+        outs.extend(o)
+    return torch.cat(lens), outs

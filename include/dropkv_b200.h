@@ -26,6 +26,8 @@
  *   dropkv_gather          <- dropkv_cache.py:479-491   DropKVCache._gather_compressed
  *   dropkv_compress        <- dropkv_cache.py:355-491   _compute_keep_indices + _gather_compressed
  *   dropkv_compress_strided <- dropkv_cache.py:581-607  the same over in-place row buffers (no torch.cat)
+ *   dropkv_compress_varlen <- dropkv_cache.py:355-491 and 470-473, 749-788: dropkv_compress over a
+ *                             ragged batch in one call, keep_len per sequence evaluated on the device
  */
 #ifndef DROPKV_B200_H
 #define DROPKV_B200_H
@@ -199,6 +201,48 @@ DROPKV_API int dropkv_compress_strided(const void* q, int64_t q_sb, int64_t q_sh
                                        int kernel_size, int protect_window, int keep_len, float* scores_out,
                                        int64_t* keep_idx, void* k_out, void* v_out, int64_t out_head_stride,
                                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* One sequence of a ragged batch for dropkv_compress_varlen. */
+typedef struct dropkv_varlen_seq {
+  const void* q;                    /* Q [B, Hq, Lq, D] with the element strides below */
+  int64_t q_sb, q_sh, q_ss, q_sd;
+  int Lq;
+  int B;                            /* (b) rows of this sequence, e.g. its layers stacked */
+  int Lk;                           /* keys */
+  int cap;                          /* rows of room per (b, KV head) in the outputs, 1 <= cap <= Lk */
+  const void* k;                    /* K, V [B, Hkv, Lk, D], contiguous */
+  const void* v;
+  int64_t* keep_idx;                /* [B, Hkv, cap] */
+  void* k_out;                      /* [B, Hkv, cap, D] */
+  void* v_out;
+} dropkv_varlen_seq;
+
+#define DROPKV_VARLEN_MAX_SEQS 32
+
+DROPKV_API size_t dropkv_compress_varlen_workspace_size(int n_seq, const dropkv_varlen_seq* seqs, int Hq, int Hkv,
+                                                        int D, int window);
+
+/* dropkv_compress over a ragged batch of n_seq <= DROPKV_VARLEN_MAX_SEQS
+ * sequences (host array `seqs`) in one call: each sequence is scored from its
+ * last min(window, Lq) query rows (one scorer launch per sequence), then one
+ * selection launch and one gather launch cover every (sequence, b, KV head) row.
+ * keep_len of sequence s is evaluated on the device by the reference's rule
+ * (dropkv_cache.py:470-473) and written to keep_len_out[s] (int32, device):
+ *   min(Lk, max(int(keep_ratio * base), keep_window, 1)), base = total_tokens[s]
+ *   if total_tokens (int64, device, may be NULL) else Lk, then
+ *   min(max_keep_len[s]) if max_keep_len (int64, device, may be NULL; a negative
+ *   entry sets no cap), and at most cap.
+ * total_tokens / max_keep_len carry the seen-token count and the KV budget of the
+ * reference's chunked-prefill policies (dropkv_cache.py:749-788) per sequence.
+ * keep_idx / k_out / v_out rows past keep_len_out[s] are left untouched. The
+ * first 4 bytes of the workspace receive the OR of the tensor-core scorer's
+ * status words (non-zero: a bounded wait gave up). Kept sets equal those of
+ * dropkv_compress per sequence with the same keep_len. */
+DROPKV_API int dropkv_compress_varlen(int n_seq, const dropkv_varlen_seq* seqs, int dtype, int Hq, int Hkv, int D,
+                                      int window, float eps, int round_p, int kernel_size, int protect_window,
+                                      double keep_ratio, int keep_window, const int64_t* total_tokens,
+                                      const int64_t* max_keep_len, int32_t* keep_len_out, void* workspace,
+                                      size_t workspace_bytes, void* stream);
 
 /* Appends `rows` rows per (b, kv head) of K and V (src: [BH, rows, D] with
  * src_head_stride elements between heads) at row dst_row of row buffers with

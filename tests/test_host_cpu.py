@@ -53,6 +53,60 @@ def test_c_abi_rejects_bad_arguments_without_touching_the_gpu():
     assert rc == _lib.ERR_ARG and "keep_len" in lib.dropkv_last_error().decode()
 
 
+def _varlen_seqs(specs, align=4096):
+    """ctypes table of a ragged batch with placeholder (never dereferenced) pointers."""
+    seqs = (_lib.VarlenSeq * len(specs))()
+    for i, (B, Lq, Lk, cap) in enumerate(specs):
+        sq = seqs[i]
+        sq.q, sq.k, sq.v = align, 2 * align, 3 * align
+        sq.q_sb, sq.q_sh, sq.q_ss, sq.q_sd = 32 * Lq * 128, Lq * 128, 128, 1
+        sq.Lq, sq.B, sq.Lk, sq.cap = Lq, B, Lk, cap
+        sq.keep_idx, sq.k_out, sq.v_out = 4 * align, 5 * align, 6 * align
+    return seqs
+
+
+def test_varlen_workspace_layout_without_gpu():
+    lib = _lib.load()
+    specs = [(2, 8, 1000, 100), (1, 8, 70000, 7000), (3, 16, 4096, 4096)]
+    seqs = _varlen_seqs(specs)
+    n = lib.dropkv_compress_varlen_workspace_size(3, seqs, 32, 8, 128, 8)
+    scratch = max(lib.dropkv_scores_workspace_size(B, 32, 8, Lk, 128, min(8, Lq)) for B, Lq, Lk, _ in specs)
+    rows = 0
+    for B, _, Lk, _ in specs:
+        rows += -(-(B * 8 * Lk * 4) // 256) * 256  # each sequence's score rows, 256-byte aligned
+    assert n == -(-(256 + scratch) // 256) * 256 + rows
+    assert lib.dropkv_compress_varlen_workspace_size(0, seqs, 32, 8, 128, 8) == 0
+    assert lib.dropkv_compress_varlen_workspace_size(_lib.VARLEN_MAX_SEQS + 1, seqs, 32, 8, 128, 8) == 0
+
+
+@pytest.mark.parametrize("change,code,text", [
+    (dict(n=0), _lib.ERR_ARG, "n_seq"),
+    (dict(n=_lib.VARLEN_MAX_SEQS + 1), _lib.ERR_ARG, "n_seq"),
+    (dict(keep_ratio=0.0), _lib.ERR_ARG, "keep_ratio"),
+    (dict(keep_ratio=1.5), _lib.ERR_ARG, "keep_ratio"),
+    (dict(keep_ratio=float("nan")), _lib.ERR_ARG, "keep_ratio"),
+    (dict(cap=0), _lib.ERR_ARG, "cap"),
+    (dict(cap=5001), _lib.ERR_ARG, "cap"),
+    (dict(Lk=300000, cap=10), _lib.ERR_UNSUPPORTED, "one-launch selection"),
+    (dict(B=9000), _lib.ERR_ARG, "65535"),
+    (dict(k=4100), _lib.ERR_ARG, "16-byte"),
+    (dict(kernel_size=4), _lib.ERR_ARG, "odd"),
+    (dict(keep_len_out=None), _lib.ERR_ARG, "keep_len_out"),
+])
+def test_varlen_rejects_bad_arguments_without_touching_the_gpu(change, code, text):
+    lib = _lib.load()
+    B, Lk, cap = change.get("B", 1), change.get("Lk", 5000), change.get("cap", 500)
+    seqs = _varlen_seqs([(1, 8, 1000, 100), (B, 8, Lk, cap)])
+    if "k" in change:
+        seqs[1].k = change["k"]
+    n = change.get("n", 2)
+    rc = lib.dropkv_compress_varlen(n, seqs, _lib.DTYPE_BF16, 32, 8, 128, 8, 1e-6, _lib.ROUND_BF16,
+                                    change.get("kernel_size", 11), 8, change.get("keep_ratio", 0.1), 8, None,
+                                    None, change.get("keep_len_out", 4096), None, 0, None)
+    assert rc == code
+    assert text in lib.dropkv_last_error().decode()
+
+
 def _mk(B=1, Hq=32, Hkv=8, Lq=64, Lk=64, D=128, dtype=torch.bfloat16):
     return (torch.randn(B, Hq, Lq, D).to(dtype), torch.randn(B, Hkv, Lk, D).to(dtype),
             torch.randn(B, Hkv, Lk, D).to(dtype))
