@@ -108,9 +108,11 @@ def parse_args():
     ap.add_argument("--ragged-partition", choices=["contiguous", "lpt"], default="contiguous",
                     help="ragged: units cut into consecutive (sequence, layer) runs of equal work, or "
                          "longest-first to the least loaded rank (dropkv_b200.sharding)")
-    ap.add_argument("--ragged-batch", choices=["sequence", "unit"], default="sequence",
-                    help="ragged: one compress call per sequence over the rank's layers of it "
-                         "(B = layers), or one call per (sequence, layer) unit")
+    ap.add_argument("--ragged-batch", choices=["varlen", "sequence", "unit"], default="varlen",
+                    help="ragged: one dropkv_compress_varlen call over all the rank's sequences "
+                         "(keep_len per sequence on the device; default), one compress call per "
+                         "sequence over the rank's layers of it (B = layers), or one call per "
+                         "(sequence, layer) unit")
     return ap.parse_args()
 
 
@@ -762,13 +764,34 @@ def ragged_record(args, rank, n, world, dev, ratios=RAGGED_RATIOS, steps=5, warm
     by_ratio, launches = {}, 0
     for kr in ratios:
         comps = []
-        for lk, (Q, K, V) in work:
-            comps.append((ops.Compressor(Q.shape[0], Q.shape[1], K.shape[1], Q.shape[2], lk, Q.shape[3], Q.dtype,
-                                         8, 11, keep_len_rule(lk, kr, 8), device=dev), (Q, K, V)))
+        if args.ragged_batch == "varlen":
+            # one call per VARLEN_MAX_SEQS sequences (a rank holds at most 16 here:
+            # one call); the outputs are sized by the host rule, which the device
+            # keep_len must reproduce
+            step = _lib.VARLEN_MAX_SEQS
+            for a in range(0, len(work), step):
+                part = work[a:a + step]
+                shapes = [(Q.shape[0], Q.shape[2], lk) for lk, (Q, K, V) in part]
+                caps = [keep_len_rule(lk, kr, 8) for lk, _ in part]
+                vc = ops.VarlenCompressor(shapes, 32, 8, 128, part[0][1][0].dtype, 8, 11, kr, caps=caps,
+                                          device=dev)
+                qkv = ([q for _, (q, _, _) in part], [k for _, (_, k, _) in part], [v for _, (_, _, v) in part])
+                kl, _ = vc.run(*qkv)
+                if kl.cpu().tolist() != caps:
+                    raise RuntimeError(f"device keep_len {kl.cpu().tolist()} != host rule {caps}")
+                comps.append((vc, qkv))
 
-        def one_pass():
-            for comp, (Q, K, V) in comps:
-                comp.run(Q, K, V)
+            def one_pass():
+                for vc, qkv in comps:
+                    vc.run(*qkv)
+        else:
+            for lk, (Q, K, V) in work:
+                comps.append((ops.Compressor(Q.shape[0], Q.shape[1], K.shape[1], Q.shape[2], lk, Q.shape[3],
+                                             Q.dtype, 8, 11, keep_len_rule(lk, kr, 8), device=dev), (Q, K, V)))
+
+            def one_pass():
+                for comp, (Q, K, V) in comps:
+                    comp.run(Q, K, V)
 
         for _ in range(warmup):
             one_pass()
@@ -806,7 +829,8 @@ def ragged_record(args, rank, n, world, dev, ratios=RAGGED_RATIOS, steps=5, warm
                    "units_per_rank": [len(p) for p in parts], "planned_imbalance": load_imbalance(parts),
                    "partition": args.ragged_partition, "batching": args.ragged_batch,
                    "calls_per_pass_rank0": len(ragged_plan(args, n)[2][0]) if args.ragged_batch == "unit"
-                   else len({u.seq for u in parts[0]}),
+                   else (-(-len({u.seq for u in parts[0]}) // 32) if args.ragged_batch == "varlen"
+                         else len({u.seq for u in parts[0]})),
                    "parallelism": f"{n} ranks, (sequence, layer) units, {args.ragged_partition} partition, "
                                   "no collective",
                    "timing": "CUDA events per rank after a barrier, max over ranks",
