@@ -67,6 +67,10 @@ SIGNATURES = {
                                  _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int,
                                  _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz,
                                  _c_p]),
+    "dropkv_compress_kv_strides": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_i64,
+                                            _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                            _c_f, _c_int, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                            _c_sz, _c_p]),
     "dropkv_compress_varlen_workspace_size": (_c_sz, [_c_int, ctypes.POINTER(VarlenSeq), _c_int, _c_int, _c_int,
                                                       _c_int]),
     "dropkv_compress_varlen": (_c_int, [_c_int, ctypes.POINTER(VarlenSeq), _c_int, _c_int, _c_int, _c_int, _c_int,

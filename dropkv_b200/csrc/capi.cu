@@ -117,7 +117,7 @@ static ScoreProblem make_problem(const void* q, int64_t q_sb, int64_t q_sh, int6
                                  int D, int window, float eps, int round_p, float* scores) {
   ScoreProblem p;
   p.q = q; p.q_sb = q_sb; p.q_sh = q_sh; p.q_ss = q_ss; p.q_sd = q_sd; p.Lq = Lq;
-  p.k = k; p.v = v; p.kv_sh = (int64_t)Lk * D; p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.Lk = Lk; p.D = D;
+  p.k = k; p.v = v; p.kv_sh = (int64_t)Lk * D; p.kv_sb = (int64_t)Hkv * Lk * D; p.kv_ss = D; p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.Lk = Lk; p.D = D;
   p.W = window; p.g = Hq / Hkv; p.M = p.g * window;
   p.scale = (float)(1.0 / std::sqrt((double)D));
   p.eps = eps; p.round_mode = round_p; p.scores = scores; p.status = nullptr;
@@ -149,6 +149,9 @@ static int run_scores(const ScoreProblem& p, int dtype, void* ws, cudaStream_t s
   if (use_tc(dtype, p.B, p.Hkv, p.Lk, p.M, p.D)) return launch_scores_tc(p, dtype, ws, st);
   if (g_backend.load(std::memory_order_relaxed) == 2)
     return fail(DROPKV_ERR_UNSUPPORTED, "tensor-core scorer forced but it does not cover this problem");
+  if (p.kv_ss != p.D || p.kv_sb != (int64_t)p.Hkv * p.kv_sh)
+    return fail(DROPKV_ERR_UNSUPPORTED, "the CUDA-core scorer (fp32, D 32/256, M > 64) needs K/V rows packed "
+                                        "per (sequence, head); copy K and V to that layout first");
   ScorePlan plan = plan_scores(p.B, p.Hkv, p.Lk, p.M, p.D);
   return launch_scores_simt(p, plan, ws, st, dtype);
 }
@@ -390,6 +393,7 @@ int dropkv_compress_strided(const void* q, int64_t q_sb, int64_t q_sh, int64_t q
   ScoreProblem p = make_problem(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, B, Hq, Hkv, Lk, D, window, eps,
                                 round_p, scores);
   p.kv_sh = kv_head_stride;
+  p.kv_sb = (int64_t)Hkv * kv_head_stride;
   if ((rc = run_scores(p, dtype, workspace, st))) return rc;
   int protect = std::min(protect_window, Lk);
   if (select_gather_supported(Lk, kernel_size))
@@ -399,6 +403,42 @@ int dropkv_compress_strided(const void* q, int64_t q_sb, int64_t q_sh, int64_t q
   return launch_gather(k, v, elem_bytes_of(dtype), B * Hkv, Lk, D, keep_idx, keep_len, k_out, v_out, st,
                        kv_head_stride, out_head_stride);
 }
+
+int dropkv_compress_kv_strides(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                               const void* k, const void* v, int64_t kv_sb, int64_t kv_sh, int64_t kv_ss,
+                               int dtype, int B, int Hq, int Hkv, int Lk, int D, int window, float eps, int round_p,
+                               int kernel_size, int protect_window, int keep_len, float* scores_out,
+                               int64_t* keep_idx, void* k_out, void* v_out, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  int rc = check_score_args(q, Lq, k, v, dtype, B, Hq, Hkv, Lk, D, window, round_p);
+  if (rc) return rc;
+  if ((rc = check_select_args(B, Hkv, Lk, kernel_size, protect_window, keep_len))) return rc;
+  if (!keep_idx || !k_out || !v_out) return fail(DROPKV_ERR_ARG, "keep_idx, k_out and v_out must be non-NULL");
+  const int eb = elem_bytes_of(dtype);
+  if (kv_ss < D || kv_sh < 1 || kv_sb < 1 || (kv_ss * eb) % 16 || (kv_sh * eb) % 16 || (kv_sb * eb) % 16)
+    return fail(DROPKV_ERR_ARG, "K/V strides (%lld, %lld, %lld) must be positive multiples of 16 bytes with rows "
+                "of D=%d contiguous elements", (long long)kv_sb, (long long)kv_sh, (long long)kv_ss, D);
+  size_t s_ws = dropkv_scores_workspace_size(B, Hq, Hkv, Lk, D, window);
+  size_t need = dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, window);
+  if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
+  char* base = reinterpret_cast<char*>(workspace);
+  float* scores = scores_out ? scores_out : reinterpret_cast<float*>(base + s_ws);
+  void* sel_ws = base + s_ws + align_up((size_t)B * Hkv * Lk * 4, 256);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ScoreProblem p = make_problem(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, B, Hq, Hkv, Lk, D, window, eps,
+                                round_p, scores);
+  p.kv_sb = kv_sb;
+  p.kv_sh = kv_sh;
+  p.kv_ss = kv_ss;
+  if ((rc = run_scores(p, dtype, workspace, st))) return rc;
+  int protect = std::min(protect_window, Lk);
+  if (select_gather_supported(Lk, kernel_size))
+    return launch_select_gather(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, k, v, eb, D, k_out,
+                                v_out, st, kv_sh, 0, Hkv, kv_sb, kv_ss);
+  if ((rc = launch_select(scores, B * Hkv, Lk, kernel_size, protect, keep_len, keep_idx, sel_ws, st))) return rc;
+  return launch_gather(k, v, eb, B * Hkv, Lk, D, keep_idx, keep_len, k_out, v_out, st, kv_sh, 0, Hkv, kv_sb, kv_ss);
+}
+
 
 int dropkv_append_rows(void* k_dst, void* v_dst, int64_t dst_head_stride, int dst_row, const void* k_src,
                        const void* v_src, int64_t src_head_stride, int rows, int D, int elem_bytes, int BH,

@@ -71,7 +71,9 @@ struct ScoreProblem {
   int Lq;
   const void* k;
   const void* v;
-  int64_t kv_sh;  // elements between consecutive (b, kv head) rows of K and V (Lk * D if contiguous)
+  int64_t kv_sh;  // elements between consecutive KV heads of K and V (Lk * D if contiguous)
+  int64_t kv_sb;  // elements between consecutive sequences (Hkv * kv_sh if contiguous)
+  int64_t kv_ss;  // elements between consecutive keys (D if contiguous); rows of D contiguous
   int B, Hq, Hkv, Lk, D;
   int W;       // query rows per head used (window)
   int g;       // Hq / Hkv
@@ -192,12 +194,16 @@ int launch_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q
 // k == nullptr: selection only (keep_idx), no gather
 // in_sh / out_sh: elements between consecutive heads of K/V and of K_c/V_c
 // (0: contiguous, Lk * D and keep_len * D)
+// in_sb / in_ss (0: Hkv * in_sh and D): elements between consecutive sequences
+// and keys of K/V (row bh = b * Hkv + h).
 int launch_select_gather(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
                          int64_t* keep_idx, const void* k, const void* v, int elem_bytes, int D, void* ko,
-                         void* vo, cudaStream_t st, int64_t in_sh = 0, int64_t out_sh = 0);
+                         void* vo, cudaStream_t st, int64_t in_sh = 0, int64_t out_sh = 0, int Hkv = 1,
+                         int64_t in_sb = 0, int64_t in_ss = 0);
 int launch_gather(const void* k, const void* v, int elem_bytes, int BH, int Lk, int D,
                   const int64_t* keep_idx, int keep_len, void* k_out, void* v_out,
-                  cudaStream_t st, int64_t in_sh = 0, int64_t out_sh = 0);
+                  cudaStream_t st, int64_t in_sh = 0, int64_t out_sh = 0, int Hkv = 1, int64_t in_sb = 0,
+                  int64_t in_ss = 0);
 // A ragged batch: one selection launch and one gather launch over every row of
 // the table (t.scores filled); the longest row must pass select_gather_supported.
 int launch_select_gather_varlen(const VarlenTable& t, int kernel_size, int elem_bytes, int D, cudaStream_t st);

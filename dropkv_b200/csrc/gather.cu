@@ -16,13 +16,13 @@ constexpr int GT_NT = 256;  // threads per block
 constexpr int GT_U = 2;     // chunks per thread and step: 2 K and 2 V loads in flight
 
 // One row: ko[i, :] = kb[ib[i], :] and vo[i, :] = vb[ib[i], :] for i < keep_len, rows
-// of CR vectors. Block x of the row handles steps x, x + gridDim.x, ...; a step is
-// GT_U * GT_NT consecutive chunks, and all its index and data loads are issued
-// before its stores.
+// of CR vectors, input rows RS vectors apart. Block x of the row handles steps x,
+// x + gridDim.x, ...; a step is GT_U * GT_NT consecutive chunks, and all its index
+// and data loads are issued before its stores.
 template <typename VT>
 __device__ __forceinline__ void gather_row(const VT* __restrict__ kb, const VT* __restrict__ vb,
                                            const int64_t* __restrict__ ib, int Lk, int keep_len, int CR,
-                                           VT* __restrict__ kob, VT* __restrict__ vob) {
+                                           VT* __restrict__ kob, VT* __restrict__ vob, int64_t RS) {
   const int64_t n = (int64_t)keep_len * CR;
   for (int64_t c0 = (int64_t)blockIdx.x * (GT_U * GT_NT) + threadIdx.x; c0 < n;
        c0 += (int64_t)gridDim.x * (GT_U * GT_NT)) {
@@ -39,8 +39,8 @@ __device__ __forceinline__ void gather_row(const VT* __restrict__ kb, const VT* 
 #pragma unroll
     for (int u = 0; u < GT_U; ++u) {
       if (src[u] >= 0 && src[u] < Lk) {
-        a[u] = kb[src[u] * CR + col[u]];
-        b[u] = vb[src[u] * CR + col[u]];
+        a[u] = kb[src[u] * RS + col[u]];
+        b[u] = vb[src[u] * RS + col[u]];
       } else {
         a[u] = VT{};
         b[u] = VT{};
@@ -56,16 +56,20 @@ __device__ __forceinline__ void gather_row(const VT* __restrict__ kb, const VT* 
   }
 }
 
-// in_sh / out_sh: vectors between consecutive heads of the input and the output.
+// Row bh = b * Hkv + h; in_sb / in_sh / in_rs: vectors between consecutive
+// sequences, heads and keys of the input; out_sh: between consecutive rows of the
+// output.
 template <typename VT>
 __global__ void __launch_bounds__(GT_NT) gather_kernel(const VT* __restrict__ k, const VT* __restrict__ v,
                                                        const int64_t* __restrict__ idx, int Lk, int keep_len,
-                                                       int CR, VT* __restrict__ ko, VT* __restrict__ vo,
-                                                       int64_t in_sh, int64_t out_sh) {
+                                                       int CR, VT* __restrict__ ko, VT* __restrict__ vo, int Hkv,
+                                                       int64_t in_sb, int64_t in_sh, int64_t in_rs,
+                                                       int64_t out_sh) {
   const int bh = blockIdx.y;
+  const int64_t in_off = (int64_t)(bh / Hkv) * in_sb + (int64_t)(bh % Hkv) * in_sh;
   pdl_wait();  // keep_idx may come from the kernel before this one
-  gather_row<VT>(k + (size_t)bh * in_sh, v + (size_t)bh * in_sh, idx + (size_t)bh * keep_len, Lk, keep_len, CR,
-                 ko + (size_t)bh * out_sh, vo + (size_t)bh * out_sh);
+  gather_row<VT>(k + in_off, v + in_off, idx + (size_t)bh * keep_len, Lk, keep_len, CR, ko + (size_t)bh * out_sh,
+                 vo + (size_t)bh * out_sh, in_rs);
 }
 
 // A ragged batch: row blockIdx.y of the table's batch, with its sequence's
@@ -81,12 +85,13 @@ __global__ void __launch_bounds__(GT_NT) gather_varlen_kernel(const __grid_const
   const int64_t in_sh = (int64_t)q.lk * CR, out_sh = (int64_t)q.cap * CR;
   gather_row<VT>(reinterpret_cast<const VT*>(q.k) + b * in_sh, reinterpret_cast<const VT*>(q.v) + b * in_sh,
                  q.keep_idx + (size_t)b * q.cap, q.lk, keep_len, CR, reinterpret_cast<VT*>(q.k_out) + b * out_sh,
-                 reinterpret_cast<VT*>(q.v_out) + b * out_sh);
+                 reinterpret_cast<VT*>(q.v_out) + b * out_sh, CR);
 }
 
 template <typename VT>
 int launch_vec(const void* k, const void* v, int BH, int Lk, int row_bytes, const int64_t* idx,
-               int keep_len, void* ko, void* vo, cudaStream_t st, int64_t in_sh_bytes, int64_t out_sh_bytes) {
+               int keep_len, void* ko, void* vo, cudaStream_t st, int64_t in_sh_bytes, int64_t out_sh_bytes,
+               int Hkv, int64_t in_sb_bytes, int64_t in_rs_bytes) {
   int CR = row_bytes / (int)sizeof(VT);
   int64_t n = (int64_t)keep_len * CR;
   // one wave of blocks over the GPU (8 per SM), with the steps of a row spread
@@ -109,8 +114,9 @@ int launch_vec(const void* k, const void* v, int BH, int Lk, int row_bytes, cons
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gather_kernel<VT>, reinterpret_cast<const VT*>(k),
                                      reinterpret_cast<const VT*>(v), idx, Lk, keep_len, CR,
-                                     reinterpret_cast<VT*>(ko), reinterpret_cast<VT*>(vo),
-                                     in_sh_bytes / (int64_t)sizeof(VT), out_sh_bytes / (int64_t)sizeof(VT));
+                                     reinterpret_cast<VT*>(ko), reinterpret_cast<VT*>(vo), Hkv,
+                                     in_sb_bytes / (int64_t)sizeof(VT), in_sh_bytes / (int64_t)sizeof(VT),
+                                     in_rs_bytes / (int64_t)sizeof(VT), out_sh_bytes / (int64_t)sizeof(VT));
   if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "gather launch: %s", cudaGetErrorString(e));
   return check_launch("gather");
 }
@@ -148,19 +154,30 @@ int launch_varlen_vec(const VarlenTable& t, int row_bytes, cudaStream_t st) {
 
 int launch_gather(const void* k, const void* v, int elem_bytes, int BH, int Lk, int D,
                   const int64_t* keep_idx, int keep_len, void* k_out, void* v_out, cudaStream_t st,
-                  int64_t in_sh, int64_t out_sh) {
+                  int64_t in_sh, int64_t out_sh, int Hkv, int64_t in_sb, int64_t in_ss) {
   if (keep_len == 0 || BH == 0) return DROPKV_OK;
   const int row_bytes = D * elem_bytes;
-  const int64_t in_b = (in_sh ? in_sh : (int64_t)Lk * D) * elem_bytes;
+  const int64_t sh = in_sh ? in_sh : (int64_t)Lk * D;
+  const int64_t in_b = sh * elem_bytes;
+  const int64_t sb_b = (in_sb ? in_sb : (int64_t)Hkv * sh) * elem_bytes;
+  const int64_t rs_b = (in_ss ? in_ss : (int64_t)D) * elem_bytes;
   const int64_t out_b = (out_sh ? out_sh : (int64_t)keep_len * D) * elem_bytes;
   for (int w : {16, 8, 4, 2}) {
-    if (row_bytes % w == 0 && in_b % w == 0 && out_b % w == 0 && aligned(k, w) && aligned(v, w) &&
-        aligned(k_out, w) && aligned(v_out, w)) {
+    if (row_bytes % w == 0 && in_b % w == 0 && sb_b % w == 0 && rs_b % w == 0 && out_b % w == 0 && aligned(k, w) &&
+        aligned(v, w) && aligned(k_out, w) && aligned(v_out, w)) {
       switch (w) {
-        case 16: return launch_vec<uint4>(k, v, BH, Lk, row_bytes, keep_idx, keep_len, k_out, v_out, st, in_b, out_b);
-        case 8: return launch_vec<uint2>(k, v, BH, Lk, row_bytes, keep_idx, keep_len, k_out, v_out, st, in_b, out_b);
-        case 4: return launch_vec<uint32_t>(k, v, BH, Lk, row_bytes, keep_idx, keep_len, k_out, v_out, st, in_b, out_b);
-        case 2: return launch_vec<uint16_t>(k, v, BH, Lk, row_bytes, keep_idx, keep_len, k_out, v_out, st, in_b, out_b);
+        case 16:
+          return launch_vec<uint4>(k, v, BH, Lk, row_bytes, keep_idx, keep_len, k_out, v_out, st, in_b, out_b, Hkv,
+                                   sb_b, rs_b);
+        case 8:
+          return launch_vec<uint2>(k, v, BH, Lk, row_bytes, keep_idx, keep_len, k_out, v_out, st, in_b, out_b, Hkv,
+                                   sb_b, rs_b);
+        case 4:
+          return launch_vec<uint32_t>(k, v, BH, Lk, row_bytes, keep_idx, keep_len, k_out, v_out, st, in_b, out_b,
+                                      Hkv, sb_b, rs_b);
+        case 2:
+          return launch_vec<uint16_t>(k, v, BH, Lk, row_bytes, keep_idx, keep_len, k_out, v_out, st, in_b, out_b,
+                                      Hkv, sb_b, rs_b);
       }
     }
   }

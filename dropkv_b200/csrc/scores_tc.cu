@@ -81,6 +81,24 @@ int make_kv_tensor_map(CUtensorMap* map, const void* base, int BH, int L, int D,
   return DROPKV_OK;
 }
 
+int make_kv_tensor_map_4d(CUtensorMap* map, const void* base, int B, int Hkv, int L, int D, bool bf16, int64_t sb,
+                          int64_t sh, int64_t ss) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(DROPKV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  if (reinterpret_cast<uintptr_t>(base) % 16) return fail(DROPKV_ERR_ARG, "K/V must be 16-byte aligned");
+  if ((sb * 2) % 16 || (sh * 2) % 16 || (ss * 2) % 16)
+    return fail(DROPKV_ERR_ARG, "K/V strides must be multiples of 8 elements");
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)L, (cuuint64_t)Hkv, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)ss * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DROPKV_ERR_CUDA, "cuTensorMapEncodeTiled (4-D K/V) failed (%d)", (int)r);
+  return DROPKV_OK;
+}
+
 // Q viewed as {D, Lq, Hq, B} with box {64, W, g, 1}: one load per 64-wide slab
 // brings the W window rows of the g query heads of one KV head, in the order of
 // the scorer's query rows (m = head * W + row), under the 128-byte swizzle.
@@ -517,8 +535,9 @@ __global__ void __launch_bounds__(NTH, 1)
         const int bh = r * a.groups + grp;
         tc::mbar_arrive_expect_tx(&full[slot], L::TILE);
         for (int rr = 0; rr < NREG; ++rr)
-          tc::tma_load_3d(sm + L::RING + slot * L::TILE + rr * 16384, stage == 0 ? &kmap : &vmap, &full[slot],
-                          64 * rr, (t0 + tile) * TK, bh, stage == 1 ? pol_last : pol_first);
+          tc::tma_load_4d_hint(sm + L::RING + slot * L::TILE + rr * 16384, stage == 0 ? &kmap : &vmap,
+                               &full[slot], 64 * rr, (t0 + tile) * TK, bh % p.Hkv, bh / p.Hkv,
+                               stage == 1 ? pol_last : pol_first);
       }
       // every issued copy has landed before the CTA may exit (already true unless
       // a wait gave up)
@@ -1172,9 +1191,9 @@ static int launch_fused_t(const ScoreProblem& p, const TcPlan& t, void* ws, cuda
   CUtensorMap km, vm;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   const int BH = p.B * p.Hkv;
-  int rc = make_kv_tensor_map(&km, p.k, BH, p.Lk, D, bf16, p.kv_sh);
+  int rc = make_kv_tensor_map_4d(&km, p.k, p.B, p.Hkv, p.Lk, D, bf16, p.kv_sb, p.kv_sh, p.kv_ss);
   if (rc) return rc;
-  rc = make_kv_tensor_map(&vm, p.v, BH, p.Lk, D, bf16, p.kv_sh);
+  rc = make_kv_tensor_map_4d(&vm, p.v, p.B, p.Hkv, p.Lk, D, bf16, p.kv_sb, p.kv_sh, p.kv_ss);
   if (rc) return rc;
   CUtensorMap qm;
   std::memset(&qm, 0, sizeof(qm));

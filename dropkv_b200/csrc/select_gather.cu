@@ -640,10 +640,11 @@ static int launch_cluster_select(const float* scores, int BH, int Lk, int kernel
 // Selection into keep_idx and, when K/V are given, the gather of the kept rows.
 int launch_select_gather(const float* scores, int BH, int Lk, int kernel_size, int protect, int keep_len,
                          int64_t* keep_idx, const void* k, const void* v, int elem_bytes, int D, void* ko,
-                         void* vo, cudaStream_t st, int64_t in_sh, int64_t out_sh) {
+                         void* vo, cudaStream_t st, int64_t in_sh, int64_t out_sh, int Hkv, int64_t in_sb,
+                         int64_t in_ss) {
   int rc = launch_cluster_select(scores, BH, Lk, kernel_size, protect, keep_len, keep_idx, st);
   if (rc || k == nullptr) return rc;
-  return launch_gather(k, v, elem_bytes, BH, Lk, D, keep_idx, keep_len, ko, vo, st, in_sh, out_sh);
+  return launch_gather(k, v, elem_bytes, BH, Lk, D, keep_idx, keep_len, ko, vo, st, in_sh, out_sh, Hkv, in_sb, in_ss);
 }
 
 int launch_gather_varlen(const VarlenTable& t, int elem_bytes, int D, cudaStream_t st);

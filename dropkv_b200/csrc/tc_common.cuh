@@ -115,6 +115,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* map, uint64_t
       : "memory");
 }
 
+// 4-D tile load with an L2 cache hint.
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const void* map, uint64_t* bar, int c0, int c1, int c2,
+                                                 int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
+      : "memory");
+}
+
 // 3-D tile prefetch into L2 only: no shared memory, no completion signal.
 __device__ __forceinline__ void tma_prefetch_l2_3d(const void* map, int c0, int c1, int c2, uint64_t policy) {
   asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile.L2::cache_hint [%0, {%1, %2, %3}], %4;" ::"l"(map),
@@ -286,5 +296,9 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a
 // box {64 elements, 128 rows, 1}, 128-byte swizzle, out-of-range rows zero-filled.
 // head_stride: elements between consecutive [L, D] heads (0: L * D, contiguous).
 int make_kv_tensor_map(CUtensorMap* map, const void* base, int BH, int L, int D, bool bf16, int64_t head_stride = 0);
+// K or V [B, Hkv, L, D] with element strides (sb, sh, ss) and rows of D contiguous
+// elements, as a 4-D map {d, key, head, b} of 64 x 128 boxes (128-byte swizzle).
+int make_kv_tensor_map_4d(CUtensorMap* map, const void* base, int B, int Hkv, int L, int D, bool bf16, int64_t sb,
+                          int64_t sh, int64_t ss);
 
 }  // namespace dropkv

@@ -174,6 +174,32 @@ def gather_compressed(K: torch.Tensor, V: torch.Tensor, keep_idx: torch.Tensor):
     return Kc, Vc
 
 
+def _kv_strides(K: torch.Tensor, V: torch.Tensor):
+    """Element strides (sequence, head, key) shared by K and V [B, Hkv, L, D] when
+    their rows of D elements are contiguous, every stride is a multiple of 16 bytes
+    and both start on a 16-byte boundary; else None. Size-1 dimensions take the
+    packed stride, which their real stride cannot contradict."""
+    if K.shape != V.shape or K.dim() != 4 or K.stride(3) != 1 or V.stride(3) != 1:
+        return None
+    B, Hkv, L, D = K.shape
+    out = []
+    for T in (K, V):
+        sb, sh, ss, _ = T.stride()
+        ss = D if L == 1 else ss
+        sh = L * ss if Hkv == 1 else sh
+        sb = Hkv * sh if B == 1 else sb
+        out.append((sb, sh, ss))
+    if out[0] != out[1]:
+        return None
+    sb, sh, ss = out[0]
+    eb = K.element_size()
+    if ss < D or min(sb, sh) < 1 or any((x * eb) % 16 for x in (sb, sh, ss)):
+        return None
+    if K.data_ptr() % 16 or V.data_ptr() % 16:
+        return None
+    return sb, sh, ss
+
+
 def compress(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int, kernel_size: int,
              keep_len: int, protect_window: int | None = None, eps: float = 1e-6,
              round_p: bool = True, return_scores: bool = False):
@@ -189,8 +215,15 @@ def compress(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int, ker
     dt = _DTYPE_CODE.get(Q.dtype)
     if dt is None or K.dtype != Q.dtype or V.dtype != Q.dtype:
         raise TypeError(f"Q, K, V must share one of fp32/fp16/bf16; got {Q.dtype}, {K.dtype}, {V.dtype}")
-    K = K.contiguous()
-    V = V.contiguous()
+    # K/V views of another layout (a model's [B, L, Hkv, D] projections viewed as
+    # [B, Hkv, L, D]) are read in place when the tensor-core scorer serves the
+    # problem; otherwise they are packed first
+    strides = None if (K.is_contiguous() and V.is_contiguous()) else _kv_strides(K, V)
+    if strides is not None and scorer_for(Q.dtype, B, Hq, Hkv, Lk, D, min(int(window), Lq)) != "tensor_cores":
+        strides = None
+    if strides is None:
+        K = K.contiguous()
+        V = V.contiguous()
     pw = window if protect_window is None else protect_window
     lib = _lib.load()
     dev = Q.device
@@ -200,14 +233,18 @@ def compress(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int, ker
         Vc = torch.empty_like(Kc)
         sc = torch.empty(B, Hkv, Lk, dtype=torch.float32, device=dev) if return_scores else None
         ws = _workspace(lib.dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, int(window)), dev)
-        rc = lib.dropkv_compress(Q.data_ptr(), *Q.stride(), Lq, K.data_ptr(), V.data_ptr(), dt,
-                                 B, Hq, Hkv, Lk, D, int(window), float(eps),
-                                 _ROUND_CODE[Q.dtype] if round_p else _lib.ROUND_NONE,
-                                 int(kernel_size), int(pw), int(keep_len),
-                                 sc.data_ptr() if sc is not None else None,
-                                 idx.data_ptr(), Kc.data_ptr(), Vc.data_ptr(),
-                                 ws.data_ptr(), ws.numel(), _stream(dev))
-        _lib.check(rc, "dropkv_compress")
+        rnd = _ROUND_CODE[Q.dtype] if round_p else _lib.ROUND_NONE
+        tail = (int(kernel_size), int(pw), int(keep_len), sc.data_ptr() if sc is not None else None,
+                idx.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
+        if strides is None:
+            rc = lib.dropkv_compress(Q.data_ptr(), *Q.stride(), Lq, K.data_ptr(), V.data_ptr(), dt,
+                                     B, Hq, Hkv, Lk, D, int(window), float(eps), rnd, *tail)
+            _lib.check(rc, "dropkv_compress")
+        else:
+            rc = lib.dropkv_compress_kv_strides(Q.data_ptr(), *Q.stride(), Lq, K.data_ptr(), V.data_ptr(),
+                                                *strides, dt, B, Hq, Hkv, Lk, D, int(window), float(eps), rnd,
+                                                *tail)
+            _lib.check(rc, "dropkv_compress_kv_strides")
         if _CHECK_STATUS:
             _check_status(ws, dt, B, Hq, Hkv, Lk, D, window, "dropkv_compress")
     if return_scores:

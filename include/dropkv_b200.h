@@ -26,6 +26,7 @@
  *   dropkv_gather          <- dropkv_cache.py:479-491   DropKVCache._gather_compressed
  *   dropkv_compress        <- dropkv_cache.py:355-491   _compute_keep_indices + _gather_compressed
  *   dropkv_compress_strided <- dropkv_cache.py:581-607  the same over in-place row buffers (no torch.cat)
+ *   dropkv_compress_kv_strides <- dropkv_cache.py:355-491  the same over K/V views of any row-contiguous layout
  *   dropkv_compress_varlen <- dropkv_cache.py:355-491 and 470-473, 749-788: dropkv_compress over a
  *                             ragged batch in one call, keep_len per sequence evaluated on the device
  */
@@ -243,6 +244,22 @@ DROPKV_API int dropkv_compress_varlen(int n_seq, const dropkv_varlen_seq* seqs, 
                                       double keep_ratio, int keep_window, const int64_t* total_tokens,
                                       const int64_t* max_keep_len, int32_t* keep_len_out, void* workspace,
                                       size_t workspace_bytes, void* stream);
+
+/* dropkv_compress over K and V of any layout whose rows of D elements are
+ * contiguous: element strides kv_sb (sequence), kv_sh (KV head) and kv_ss (key),
+ * each a multiple of 16 bytes, e.g. the [B, L, Hkv, D] projections that a model's
+ * attention hands to DropKVCache.update as [B, Hkv, L, D] views
+ * (dropkv_cache.py:493-622 receive them; the reference's torch ops read any
+ * strides). Served by the tensor-core scorer (bf16/fp16, D 64/128, M <= 64);
+ * other problems need packed rows and get DROPKV_ERR_UNSUPPORTED. Outputs as
+ * dropkv_compress (K_c, V_c contiguous [B, Hkv, keep_len, D]); workspace:
+ * dropkv_compress_workspace_size. */
+DROPKV_API int dropkv_compress_kv_strides(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd,
+                                          int Lq, const void* k, const void* v, int64_t kv_sb, int64_t kv_sh,
+                                          int64_t kv_ss, int dtype, int B, int Hq, int Hkv, int Lk, int D,
+                                          int window, float eps, int round_p, int kernel_size, int protect_window,
+                                          int keep_len, float* scores_out, int64_t* keep_idx, void* k_out,
+                                          void* v_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Appends `rows` rows per (b, kv head) of K and V (src: [BH, rows, D] with
  * src_head_stride elements between heads) at row dst_row of row buffers with

@@ -107,6 +107,34 @@ def test_varlen_rejects_bad_arguments_without_touching_the_gpu(change, code, tex
     assert text in lib.dropkv_last_error().decode()
 
 
+def test_kv_stride_detection_for_model_views():
+    """A model's [B, L, Hkv, D] projections viewed as [B, Hkv, L, D] are read in
+    place (strides passed to dropkv_compress_kv_strides); layouts with split rows
+    or strides off 16-byte multiples are not."""
+    B, L, H, D = 2, 40, 4, 64
+    k = torch.zeros(B, L, H, D, dtype=torch.bfloat16).transpose(1, 2)
+    assert ops._kv_strides(k, k) == (L * H * D, D, H * D)
+    assert ops._kv_strides(k[:1], k[:1]) == (H * D, D, H * D)   # B = 1: the batch stride is moot
+    rows_split = torch.zeros(B, H, L, 2 * D, dtype=torch.bfloat16)[..., ::2]
+    assert ops._kv_strides(rows_split, rows_split) is None
+    odd = torch.zeros(B, L, H, D + 4, dtype=torch.bfloat16).transpose(1, 2)[..., :D]
+    assert ops._kv_strides(odd, odd) is None          # a row stride of 68 elements: not 16-byte aligned
+    packed = torch.zeros(B, H, L, D, dtype=torch.bfloat16)
+    assert ops._kv_strides(packed, packed) == (H * L * D, L * D, D)
+    assert ops._kv_strides(k, packed) is None         # K and V must share the layout
+
+
+def test_kv_strides_entry_rejects_bad_strides_without_touching_the_gpu():
+    lib = _lib.load()
+    base = 4096
+    for sb, sh, ss in [(0, 64, 128), (4096, 64, 60), (4096, 68, 128), (4100, 64, 128)]:
+        rc = lib.dropkv_compress_kv_strides(base, 0, 0, 0, 1, 8, base, base, sb, sh, ss, _lib.DTYPE_BF16, 1, 8, 2,
+                                            100, 64, 8, 1e-6, _lib.ROUND_BF16, 11, 8, 10, None, base, base, base,
+                                            base, 1 << 20, None)
+        assert rc == _lib.ERR_ARG, (sb, sh, ss)
+        assert "strides" in lib.dropkv_last_error().decode()
+
+
 def _mk(B=1, Hq=32, Hkv=8, Lq=64, Lk=64, D=128, dtype=torch.bfloat16):
     return (torch.randn(B, Hq, Lq, D).to(dtype), torch.randn(B, Hkv, Lk, D).to(dtype),
             torch.randn(B, Hkv, Lk, D).to(dtype))
