@@ -807,6 +807,17 @@ def ragged_record(args, rank, n, world, dev, ratios=RAGGED_RATIOS, steps=5, warm
         torch.cuda.synchronize(dev)
         launches = _lib.launch_count() - n0
         rank_ms = gather_ranks(e0.elapsed_time(e1) / steps)
+        # the timed passes did their work: every scorer status word clear
+        for comp, qkv in comps:
+            if isinstance(comp, ops.VarlenCompressor):
+                st = int(comp.workspace[:4].view(torch.int32).item())
+            else:
+                Q = qkv[0]
+                off = _lib.load().dropkv_scores_status_offset(_lib.DTYPE_BF16, Q.shape[0], Q.shape[1],
+                                                              qkv[1].shape[1], qkv[1].shape[2], Q.shape[3], 8)
+                st = 0 if off == _lib.NO_STATUS else int(comp.workspace[off:off + 4].view(torch.int32).item())
+            if st != 0:
+                raise RuntimeError(f"scorer status word {st} after the timed ragged passes: a bounded wait timed out")
         del comps
         torch.cuda.empty_cache()
         ms = max(rank_ms)
@@ -823,6 +834,8 @@ def ragged_record(args, rank, n, world, dev, ratios=RAGGED_RATIOS, steps=5, warm
     return {
         "metric": RAGGED_METRIC, "unit": UNIT, "n_gpus": n, "scaling": "strong", "steps": steps,
         "warmup": warmup, "by_keep_ratio": by_ratio,
+        "checked": "device keep_len equal to the host rule before timing; every scorer status word 0 after the "
+                   "timed passes (each rank)",
         "config": {"workload": f"ragged_b{args.ragged_seqs}_lk4096-65536_{args.ragged_layers}layers",
                    "sequences_lk": lengths, "layers": args.ragged_layers, "Hq": 32, "Hkv": 8, "D": 128,
                    "Lq": 8, "window": 8, "kernel_size": 11, "units": len(all_units),
