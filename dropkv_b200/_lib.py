@@ -122,9 +122,14 @@ SCORER_AUTO, SCORER_CUDA_CORES, SCORER_TENSOR_CORES = 0, 1, 2
 NO_STATUS = ctypes.c_size_t(-1).value
 
 
+scorer_mode = SCORER_AUTO  # the mode last set through set_scorer (keys cached per-shape plans)
+
+
 def set_scorer(mode: int) -> None:
     """Process-wide scorer choice (0 auto, 1 CUDA cores, 2 tensor cores)."""
+    global scorer_mode
     check(load().dropkv_set_scorer(int(mode)), "dropkv_set_scorer")
+    scorer_mode = int(mode)
 
 
 def launch_count() -> int:

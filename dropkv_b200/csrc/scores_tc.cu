@@ -37,6 +37,7 @@
 // fault in this logic ends the kernel instead of hanging the GPU.
 #include <atomic>
 #include <cmath>
+#include <mutex>
 #include <cstring>
 #include <type_traits>
 
@@ -1143,7 +1144,7 @@ struct TcPlan {
 
 static int tc_npad(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0; }
 
-TcPlan plan_tc(int BH, int Lk, int M, int D, int nsm) {
+static TcPlan plan_tc_compute(int BH, int Lk, int M, int D, int nsm) {
   TcPlan t;
   std::memset(&t, 0, sizeof(t));
   t.npad = tc_npad(M);
@@ -1178,6 +1179,28 @@ TcPlan plan_tc(int BH, int Lk, int M, int D, int nsm) {
   t.off_lse = off; off = align_up(off + (size_t)BH * M * 4, 256);
   t.bytes = off;
   t.ok = true;
+  return t;
+}
+
+// The plan of a problem is asked for several times per call (workspace size,
+// scorer choice, launch); the last 16 distinct problems are kept.
+TcPlan plan_tc(int BH, int Lk, int M, int D, int nsm) {
+  struct Entry {
+    int BH, Lk, M, D, nsm;
+    TcPlan t;
+  };
+  static std::mutex mu;
+  static Entry cache[16] = {};
+  static int next = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry& e : cache)
+      if (e.BH == BH && e.Lk == Lk && e.M == M && e.D == D && e.nsm == nsm) return e.t;
+  }
+  const TcPlan t = plan_tc_compute(BH, Lk, M, D, nsm);
+  std::lock_guard<std::mutex> lock(mu);
+  cache[next] = Entry{BH, Lk, M, D, nsm, t};
+  next = (next + 1) % 16;
   return t;
 }
 

@@ -19,6 +19,8 @@
 
 from __future__ import annotations
 
+import contextlib
+import functools
 import math
 import os
 
@@ -60,6 +62,24 @@ def scorer_for(dtype: torch.dtype, B, Hq, Hkv, Lk, D, window) -> str:
     """'tensor_cores' or 'cuda_cores': which scorer serves this problem."""
     r = _lib.load().dropkv_scorer_for(_DTYPE_CODE[dtype], B, Hq, Hkv, Lk, D, int(window))
     return {1: "cuda_cores", 2: "tensor_cores"}.get(r, "invalid")
+
+
+@functools.lru_cache(maxsize=4096)
+def _compress_plan(mode: int, device_index: int, dt: int, B: int, Hq: int, Hkv: int, Lk: int, D: int,
+                   window: int, score_window: int):
+    """(scorer served by the tensor cores, workspace bytes) of a compress problem on
+    the current device; the answers depend only on these values (the scorer mode,
+    the device's SM count and the shape), so they are computed once per key."""
+    lib = _lib.load()
+    tc = lib.dropkv_scorer_for(dt, B, Hq, Hkv, Lk, D, score_window) == 2
+    return tc, int(lib.dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, window))
+
+
+def _on_device(dev: torch.device):
+    """The device guard, skipped when ``dev`` is already the current device."""
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(dev)
 
 
 def _workspace(nbytes: int, device) -> torch.Tensor:
@@ -218,21 +238,23 @@ def compress(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int, ker
     # K/V views of another layout (a model's [B, L, Hkv, D] projections viewed as
     # [B, Hkv, L, D]) are read in place when the tensor-core scorer serves the
     # problem; otherwise they are packed first
-    strides = None if (K.is_contiguous() and V.is_contiguous()) else _kv_strides(K, V)
-    if strides is not None and scorer_for(Q.dtype, B, Hq, Hkv, Lk, D, min(int(window), Lq)) != "tensor_cores":
-        strides = None
-    if strides is None:
-        K = K.contiguous()
-        V = V.contiguous()
     pw = window if protect_window is None else protect_window
     lib = _lib.load()
     dev = Q.device
-    with torch.cuda.device(dev):
+    with _on_device(dev):
+        tc, nws = _compress_plan(_lib.scorer_mode, torch.cuda.current_device(), dt, B, Hq, Hkv, Lk, D, int(window),
+                                 min(int(window), Lq))
+        strides = None if (K.is_contiguous() and V.is_contiguous()) else _kv_strides(K, V)
+        if strides is not None and not tc:
+            strides = None
+        if strides is None:
+            K = K.contiguous()
+            V = V.contiguous()
         idx = torch.empty(B, Hkv, keep_len, dtype=torch.int64, device=dev)
         Kc = torch.empty(B, Hkv, keep_len, D, dtype=K.dtype, device=dev)
         Vc = torch.empty_like(Kc)
         sc = torch.empty(B, Hkv, Lk, dtype=torch.float32, device=dev) if return_scores else None
-        ws = _workspace(lib.dropkv_compress_workspace_size(B, Hq, Hkv, Lk, D, int(window)), dev)
+        ws = _workspace(nws, dev)
         rnd = _ROUND_CODE[Q.dtype] if round_p else _lib.ROUND_NONE
         tail = (int(kernel_size), int(pw), int(keep_len), sc.data_ptr() if sc is not None else None,
                 idx.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
