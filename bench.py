@@ -1060,7 +1060,9 @@ def run_decode(args):
         out = None
         for layer in range(layers):
             k, v = bufs[layer]
-            if attn == "ours":
+            if attn == "ours":  # append + attention in one launch
+                out = ops.decode_append_attention(q, kn, vn, k, v, n, workspace=ws)
+            elif attn == "split":  # the same as two calls: append, then attention
                 append(layer, n, kn, vn)
                 out = ops.decode_attention(q, k[:, :, :n + 1], v[:, :, :n + 1], workspace=ws)
             else:  # the reference: a new tensor per token, then the model's SDPA
@@ -1081,10 +1083,12 @@ def run_decode(args):
 
     for i in range(args.warmup):
         step(i, L0 + i, "ours")
+        step(i, L0 + i, "split")
         step(i, L0 + i, "sdpa")
-    # both arms start from the same cache length
+    # all arms start from the same cache length
     n0 = L0 + args.warmup
     eager_ms, launches = timed("ours", args.warmup, n0)
+    split_ms, _ = timed("split", args.warmup, n0)
     sdpa_ms, _ = timed("sdpa", args.warmup + args.steps, n0)
     # the same 32-layer step captured once and replayed (fixed cache length)
     ng = n0 + args.steps
@@ -1128,13 +1132,15 @@ def run_decode(args):
         "config": {"workload": f"decode_{layers}layers_cache{L0}", "layers": layers, "B": B, "Hq": Hq,
                    "Hkv": Hkv, "D": D, "cache_len": ng + 1, "compressed_from": args.lk,
                    "keep_ratio": args.keep_ratio, "storage": "row buffers, in-place append",
-                   "timing": "32-layer step (2 appends + 1 attention launch per layer) as a CUDA graph"},
+                   "timing": "32-layer step (1 fused append + attention launch per layer) as a CUDA graph"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                     "traffic": None, "kernel": "whole step (appends + decode attention), K/V read once",
+                     "traffic": None, "kernel": "whole step (fused append + decode attention), K/V read once",
                      "algorithmic_bytes": kv_bytes, "ms": ours_ms,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
         "eager": {"ms_per_step": eager_ms, "what": "the same calls from Python, one step after another "
                                                    "(cache length growing by one per step)"},
+        "eager_split": {"ms_per_step": split_ms, "what": "eager, the append (dropkv_append_rows) and the "
+                                                         "attention as two calls per layer"},
         "reference_path": {"ms_per_step": sdpa_ms, "what": "torch.cat of cache and token per layer "
                                                            "(dropkv_cache.py:609-617), torch SDPA (enable_gqa)"},
         "max_abs_err_vs_fp32": max_err, "cpu_baseline": None, "e2e": None, "gpu_launches": launches,

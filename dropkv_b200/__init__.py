@@ -21,14 +21,14 @@ Public API (the reference's names and semantics):
 
 from ._lib import DropKVError, version
 from .cache import DropKVCache, prefill_chunked
-from .ops import (Compressor, HostPipeline, VarlenCompressor, compress, compress_varlen, decode_attention,
-                  dropkv_scores_cuda, gather_compressed, scores, select_keep_indices)
+from .ops import (Compressor, HostPipeline, VarlenCompressor, compress, compress_varlen, decode_append_attention,
+                  decode_attention, dropkv_scores_cuda, gather_compressed, scores, select_keep_indices)
 
 # Name of the reference entry point (dropkv_triton.py:643) for drop-in imports.
 dropkv_scores_triton = dropkv_scores_cuda
 
 __all__ = [
     "DropKVCache", "prefill_chunked", "DropKVError", "version",
-    "compress", "decode_attention", "dropkv_scores_cuda", "dropkv_scores_triton", "gather_compressed",
+    "compress", "decode_attention", "decode_append_attention", "dropkv_scores_cuda", "dropkv_scores_triton", "gather_compressed",
     "scores", "select_keep_indices", "Compressor", "HostPipeline", "VarlenCompressor", "compress_varlen",
 ]

@@ -67,6 +67,9 @@ SIGNATURES = {
                                  _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int,
                                  _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p, _c_sz,
                                  _c_p]),
+    "dropkv_decode_append_attention": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_i64,
+                                                _c_i64, _c_int, _c_p, _c_p, _c_i64, _c_i64, _c_int, _c_int, _c_int,
+                                                _c_int, _c_int, _c_int, _c_f, _c_p, _c_p, _c_sz, _c_p]),
     "dropkv_compress_kv_strides": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_i64,
                                             _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                             _c_f, _c_int, _c_int, _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p,

@@ -591,5 +591,35 @@ int dropkv_compress_varlen(int n_seq, const dropkv_varlen_seq* seqs, int dtype, 
   return launch_select_gather_varlen(t, kernel_size, elem_bytes_of(dtype), D, st);
 }
 
+int dropkv_decode_append_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
+                                   const void* k_new, const void* v_new, int64_t new_sb, int64_t new_sh, int n_new,
+                                   void* k, void* v, int64_t kv_sb, int64_t kv_sh, int pos, int dtype, int B,
+                                   int Hq, int Hkv, int D, float scale, void* out, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !out || !k_new || !v_new) return fail(DROPKV_ERR_ARG, "NULL pointer argument");
+  if (dtype != DROPKV_DTYPE_BF16 && dtype != DROPKV_DTYPE_F16)
+    return fail(DROPKV_ERR_UNSUPPORTED, "decode attention takes bf16 or fp16 inputs");
+  if (D != 64 && D != 128) return fail(DROPKV_ERR_UNSUPPORTED, "decode attention needs D of 64 or 128 (got %d)", D);
+  if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv) return fail(DROPKV_ERR_ARG, "invalid head counts Hq=%d Hkv=%d", Hq, Hkv);
+  if (n_new < 1 || pos < 0) return fail(DROPKV_ERR_ARG, "need n_new >= 1 and pos >= 0 (n_new=%d, pos=%d)", n_new, pos);
+  const int L = pos + n_new;
+  if (Lq < 1 || L < Lq) return fail(DROPKV_ERR_ARG, "need 1 <= Lq <= pos + n_new (Lq=%d, L=%d)", Lq, L);
+  if ((int64_t)B * Hkv > 65535) return fail(DROPKV_ERR_ARG, "B*Hkv exceeds 65535");
+  if (kv_sh < (int64_t)L * D || kv_sb < (int64_t)Hkv * kv_sh)
+    return fail(DROPKV_ERR_ARG, "K/V buffer strides too small for %d rows", L);
+  if (new_sh < (int64_t)n_new * D || new_sb < (int64_t)Hkv * new_sh)
+    return fail(DROPKV_ERR_ARG, "new-row strides too small for %d rows", n_new);
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(k_new) |
+       reinterpret_cast<uintptr_t>(v_new)) % 16 ||
+      (kv_sh * 2) % 16 || (kv_sb * 2) % 16 || (new_sh * 2) % 16 || (new_sb * 2) % 16)
+    return fail(DROPKV_ERR_ARG, "K/V rows must start on 16-byte boundaries");
+  if (!(scale > 0.f)) return fail(DROPKV_ERR_ARG, "scale must be positive");
+  int rc = check_ws(workspace, workspace_bytes, dropkv_decode_attention_workspace_size(B, Hq, Hkv, Lq, L, D));
+  if (rc) return rc;
+  return launch_decode_attention(q, q_sb, q_sh, q_ss, q_sd, Lq, k, v, kv_sb, kv_sh, dtype, B, Hq, Hkv, L, D, scale,
+                                 out, workspace, reinterpret_cast<cudaStream_t>(stream), k_new, v_new, new_sb, new_sh,
+                                 pos);
+}
+
 }  // extern "C"
 

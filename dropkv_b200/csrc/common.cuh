@@ -188,9 +188,13 @@ bool select_gather_supported(int Lk, int kernel_size);
 
 // Decode attention over the (compressed) cache (decode_attn.cu).
 size_t decode_attention_workspace_size(int B, int Hq, int Hkv, int Lq, int L, int D);
+// k_new != nullptr: keys [pos, L) are read from k_new / v_new ([B, Hkv, L - pos, D]
+// rows with strides new_sb, new_sh) and stored into k / v at rows [pos, L).
 int launch_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
                             const void* k, const void* v, int64_t kv_sb, int64_t kv_sh, int dtype, int B, int Hq,
-                            int Hkv, int L, int D, float scale, void* out, void* ws, cudaStream_t st);
+                            int Hkv, int L, int D, float scale, void* out, void* ws, cudaStream_t st,
+                            const void* k_new = nullptr, const void* v_new = nullptr, int64_t new_sb = 0,
+                            int64_t new_sh = 0, int pos = 0);
 // k == nullptr: selection only (keep_idx), no gather
 // in_sh / out_sh: elements between consecutive heads of K/V and of K_c/V_c
 // (0: contiguous, Lk * D and keep_len * D)

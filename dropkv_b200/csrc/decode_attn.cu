@@ -74,6 +74,15 @@ struct DaArgs {
   float* part;           // [tiles][splits][8][D + 4]: output, max, sum (rows of 16-byte multiples)
   unsigned* counter;     // [tiles]
   void* out;             // [B, Hq, Lq, D]
+  // keys [pos, L) come from k_new / v_new (rows of D, strides new_sb, new_sh) and
+  // are stored into the buffers (k_buf / v_buf, the same memory as k / v) at rows
+  // [pos, L) by the first CTA of each (sequence, KV head); pos = L: no new rows
+  const void* k_new;
+  const void* v_new;
+  int64_t new_sb, new_sh;
+  int pos;
+  void* k_buf;
+  void* v_buf;
 };
 
 __device__ __forceinline__ uint4 ld_stream(const void* p) {  // read once: no L1 allocation
@@ -157,6 +166,20 @@ __global__ void __launch_bounds__(DA_NT, 1) decode_attn_kernel(DaArgs a) {
   const int m0 = tile * DA_ROWS, mvalid = min(DA_ROWS, a.M - m0);
   const T* kb = reinterpret_cast<const T*>(a.k) + b * a.kv_sb + hkv * a.kv_sh;
   const T* vb = reinterpret_cast<const T*>(a.v) + b * a.kv_sb + hkv * a.kv_sh;
+  // rows from pos on: the new rows (not yet in the buffers)
+  const T* knb = reinterpret_cast<const T*>(a.k_new) + b * a.new_sb + hkv * a.new_sh - (int64_t)a.pos * D;
+  const T* vnb = reinterpret_cast<const T*>(a.v_new) + b * a.new_sb + hkv * a.new_sh - (int64_t)a.pos * D;
+  if (a.pos < a.L && split == 0 && tile == 0) {  // append the new rows to the buffers (read from the inputs here)
+    const int nvec = (a.L - a.pos) * D / 8;
+    uint4* kd = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.k_buf) + b * a.kv_sb + hkv * a.kv_sh + (int64_t)a.pos * D);
+    uint4* vd = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.v_buf) + b * a.kv_sb + hkv * a.kv_sh + (int64_t)a.pos * D);
+    const uint4* ks = reinterpret_cast<const uint4*>(knb + (int64_t)a.pos * D);
+    const uint4* vs = reinterpret_cast<const uint4*>(vnb + (int64_t)a.pos * D);
+    for (int e = threadIdx.x; e < nvec; e += DA_NT) {
+      kd[e] = ks[e];
+      vd[e] = vs[e];
+    }
+  }
   const int j_begin = split * a.steps * DA_KS;
   const int j_end = min(a.L, j_begin + a.steps * DA_KS);
 
@@ -196,7 +219,8 @@ __global__ void __launch_bounds__(DA_NT, 1) decode_attn_kernel(DaArgs a) {
       const int j = j0 + 8 * nt + gid;
 #pragma unroll
       for (int i = 0; i < NK; ++i)
-        kr[nt][i] = j < j_end ? ld_stream(kb + (int64_t)j * D + 32 * i + 8 * tig) : make_uint4(0u, 0u, 0u, 0u);
+        kr[nt][i] = j < j_end ? ld_stream((j < a.pos ? kb : knb) + (int64_t)j * D + 32 * i + 8 * tig)
+                              : make_uint4(0u, 0u, 0u, 0u);
     }
   };
   auto load_v = [&](int j0) {
@@ -205,7 +229,8 @@ __global__ void __launch_bounds__(DA_NT, 1) decode_attn_kernel(DaArgs a) {
       const int j = j0 + 2 * tig + (r & 1) + 8 * (r >> 1);
 #pragma unroll
       for (int i = 0; i < NV; ++i)
-        vr[r][i] = j < j_end ? ld_stream(vb + (int64_t)j * D + 64 * i + 8 * gid) : make_uint4(0u, 0u, 0u, 0u);
+        vr[r][i] = j < j_end ? ld_stream((j < a.pos ? vb : vnb) + (int64_t)j * D + 64 * i + 8 * gid)
+                              : make_uint4(0u, 0u, 0u, 0u);
     }
   };
   const int jstep = DA_WARPS * DA_KS;
@@ -445,8 +470,16 @@ size_t decode_attention_workspace_size(int B, int Hq, int Hkv, int Lq, int L, in
 
 int launch_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd, int Lq,
                             const void* k, const void* v, int64_t kv_sb, int64_t kv_sh, int dtype, int B, int Hq,
-                            int Hkv, int L, int D, float scale, void* out, void* ws, cudaStream_t st) {
+                            int Hkv, int L, int D, float scale, void* out, void* ws, cudaStream_t st,
+                            const void* k_new, const void* v_new, int64_t new_sb, int64_t new_sh, int pos) {
   DaArgs a;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  a.new_sb = new_sb;
+  a.new_sh = new_sh;
+  a.pos = k_new ? pos : L;
+  a.k_buf = const_cast<void*>(k);
+  a.v_buf = const_cast<void*>(v);
   a.q = q;
   a.q_sb = q_sb;
   a.q_sh = q_sh;

@@ -382,6 +382,60 @@ def decode_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: f
     return out
 
 
+def decode_append_attention(Q: torch.Tensor, K_new: torch.Tensor, V_new: torch.Tensor, K_buf: torch.Tensor,
+                            V_buf: torch.Tensor, pos: int, scale: float | None = None,
+                            workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Append the decode rows and attend over the cache in one launch.
+
+    K_new, V_new [B, Hkv, n, D] are stored into the row buffers K_buf, V_buf
+    [B, Hkv, cap, D] at rows [pos, pos + n) and Q [B, Hq, Lq, D] attends over rows
+    [0, pos + n) -- the same output, bit for bit, as writing the rows and then
+    calling ``decode_attention(Q, K_buf[:, :, :pos + n], V_buf[:, :, :pos + n])``
+    (dropkv_cache.py:609-617 concatenate the token; the model's SDPA attends). The
+    buffers need rows of D contiguous elements and cap >= pos + n; the workspace
+    rules are those of ``decode_attention``.
+    """
+    _require_cuda(Q, K_new, V_new, K_buf, V_buf)
+    if Q.dim() != 4 or K_new.dim() != 4 or K_buf.dim() != 4 or K_new.shape != V_new.shape \
+            or K_buf.shape != V_buf.shape:
+        raise ValueError("expected Q [B,Hq,Lq,D], K_new, V_new [B,Hkv,n,D] and K_buf, V_buf [B,Hkv,cap,D]")
+    if not (Q.dtype == K_new.dtype == V_new.dtype == K_buf.dtype == V_buf.dtype) \
+            or Q.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError("decode attention takes bf16 or fp16 tensors of one dtype")
+    B, Hq, Lq, D = Q.shape
+    _, Hkv, n, _ = K_new.shape
+    cap = K_buf.shape[2]
+    pos = int(pos)
+    if K_new.shape[0] != B or K_new.shape[3] != D or K_buf.shape[0] != B or K_buf.shape[1] != Hkv \
+            or K_buf.shape[3] != D or Hq % Hkv:
+        raise ValueError(f"shape mismatch: Q {tuple(Q.shape)}, K_new {tuple(K_new.shape)}, "
+                         f"K_buf {tuple(K_buf.shape)}")
+    if pos < 0 or pos + n > cap:
+        raise ValueError(f"rows [{pos}, {pos + n}) do not fit a buffer of {cap} rows")
+    for name, t, u in (("K_buf", K_buf, V_buf), ("K_new", K_new, V_new)):
+        if t.stride() != u.stride() or t.stride(3) != 1 or (t.stride(2) != D and t.shape[2] > 1):
+            raise ValueError(f"{name} and its V need rows of D contiguous elements and equal strides")
+    scale = float(D ** -0.5 if scale is None else scale)
+    lib = _lib.load()
+    dev = Q.device
+    L = pos + n
+    need = lib.dropkv_decode_attention_workspace_size(B, Hq, Hkv, Lq, L, D)
+    if workspace is None:
+        workspace = _DA_WS.get(dev)
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.zeros(max(int(need), 1), dtype=torch.uint8, device=dev)
+            _DA_WS[dev] = workspace
+    out = torch.empty(B, Hq, Lq, D, dtype=Q.dtype, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.dropkv_decode_append_attention(Q.data_ptr(), *Q.stride(), Lq, K_new.data_ptr(), V_new.data_ptr(),
+                                                K_new.stride(0), K_new.stride(1), n, K_buf.data_ptr(),
+                                                V_buf.data_ptr(), K_buf.stride(0), K_buf.stride(1), pos,
+                                                _DTYPE_CODE[Q.dtype], B, Hq, Hkv, D, scale, out.data_ptr(),
+                                                workspace.data_ptr(), workspace.numel(), _stream(dev))
+        _lib.check(rc, "dropkv_decode_append_attention")
+    return out
+
+
 def inv_sqrt_d(D: int) -> float:
     return 1.0 / math.sqrt(D)
 

@@ -286,6 +286,21 @@ DROPKV_API int dropkv_decode_attention(const void* q, int64_t q_sb, int64_t q_sh
                                        int dtype, int B, int Hq, int Hkv, int L, int D, float scale, void* out,
                                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* dropkv_decode_attention fused with the append of the decode token(s): the
+ * n_new rows of k_new / v_new ([B, Hkv, n_new, D], element strides new_sb, new_sh,
+ * rows of D contiguous) are stored into the row buffers k / v at rows
+ * [pos, pos + n_new) and attended over together with rows [0, pos), in one launch
+ * (what dropkv_append_rows followed by dropkv_decode_attention over pos + n_new
+ * keys give, bit for bit). Replaces the decode-time cache append and attention
+ * (dropkv_cache.py:609-617 concatenate the token, the model's SDPA attends).
+ * Workspace: dropkv_decode_attention_workspace_size(B, Hq, Hkv, Lq, pos + n_new, D). */
+DROPKV_API int dropkv_decode_append_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, int64_t q_sd,
+                                              int Lq, const void* k_new, const void* v_new, int64_t new_sb,
+                                              int64_t new_sh, int n_new, void* k, void* v, int64_t kv_sb,
+                                              int64_t kv_sh, int pos, int dtype, int B, int Hq, int Hkv, int D,
+                                              float scale, void* out, void* workspace, size_t workspace_bytes,
+                                              void* stream);
+
 /* Diagnostic: one 128-row tile through a tcgen05 MMA form used by the fused
  * scorer (mode 0: out[128][n] = A[128][128] B[n][128]^T with A loaded by TMA;
  * mode 1: out[128][n] = A[128][128]^T B[n][128]^T with A read MN-major; modes 2/3:

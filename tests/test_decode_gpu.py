@@ -89,3 +89,65 @@ def test_decode_attention_rejects_bad_input():
         ops.decode_attention(Q, K, K)          # 6 query heads over 4 KV heads
     with pytest.raises(TypeError):
         ops.decode_attention(Q.float(), K.float(), K.float())
+
+
+def _split(Q, K_new, V_new, K_buf, V_buf, pos, scale=None):
+    n = K_new.shape[2]
+    K_buf[:, :, pos:pos + n] = K_new
+    V_buf[:, :, pos:pos + n] = V_new
+    return ops.decode_attention(Q, K_buf[:, :, :pos + n], V_buf[:, :, :pos + n], scale=scale)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Lq,n,pos,cap,D", [
+    (1, 32, 8, 1, 1, 13107, 13200, 128),   # the Llama decode step over the compressed cache
+    (2, 32, 8, 1, 1, 3000, 4096, 128),
+    (1, 14, 2, 1, 1, 818, 900, 64),        # Qwen2-0.5B shapes
+    (1, 16, 2, 4, 4, 777, 800, 128),       # four new rows (speculative / multi-token step)
+    (1, 8, 8, 2, 3, 0, 16, 128),           # empty cache: every key is new
+    (3, 16, 2, 1, 2, 4998, 5000, 64),      # rows up to the buffer's end
+])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_decode_append_attention_equals_append_then_attend(B, Hq, Hkv, Lq, n, pos, cap, D, dtype):
+    g = torch.Generator(device="cuda").manual_seed(pos + n + Hq)
+    Q = torch.randn(B, Hq, Lq, D, device="cuda", generator=g).to(dtype)
+    K_buf = torch.randn(B, Hkv, cap, D, device="cuda", generator=g).to(dtype)
+    V_buf = torch.randn(B, Hkv, cap, D, device="cuda", generator=g).to(dtype)
+    K_new = (torch.randn(B, Hkv, n, D, device="cuda", generator=g) * 2).to(dtype)
+    V_new = torch.randn(B, Hkv, n, D, device="cuda", generator=g).to(dtype)
+    K2, V2 = K_buf.clone(), V_buf.clone()
+    want = _split(Q, K_new, V_new, K2, V2, pos)
+    got = ops.decode_append_attention(Q, K_new, V_new, K_buf, V_buf, pos)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)                 # bit-identical to the two-call path
+    assert torch.equal(K_buf, K2) and torch.equal(V_buf, V2)   # rows stored, nothing else touched
+    ref = _reference(Q, K_buf[:, :, :pos + n], V_buf[:, :, :pos + n], D ** -0.5)
+    torch.testing.assert_close(got.float(), ref, rtol=2e-2, atol=2e-3)
+
+
+def test_decode_append_attention_from_projection_view():
+    # the token's K/V straight from a [B, 1, Hkv, D] projection (transposed view)
+    B, Hq, Hkv, D, pos, cap = 2, 32, 8, 128, 2000, 2048
+    g = torch.Generator(device="cuda").manual_seed(5)
+    Q = torch.randn(B, 1, Hq, D, device="cuda", generator=g).bfloat16().transpose(1, 2)
+    proj_k = torch.randn(B, 1, Hkv, D, device="cuda", generator=g).bfloat16()
+    proj_v = torch.randn(B, 1, Hkv, D, device="cuda", generator=g).bfloat16()
+    K_buf = torch.randn(B, Hkv, cap, D, device="cuda", generator=g).bfloat16()
+    V_buf = torch.randn(B, Hkv, cap, D, device="cuda", generator=g).bfloat16()
+    K2, V2 = K_buf.clone(), V_buf.clone()
+    kn, vn = proj_k.transpose(1, 2), proj_v.transpose(1, 2)
+    want = _split(Q, kn, vn, K2, V2, pos, scale=0.07)
+    got = ops.decode_append_attention(Q, kn, vn, K_buf, V_buf, pos, scale=0.07)
+    assert torch.equal(got, want)
+    assert torch.equal(K_buf, K2) and torch.equal(V_buf, V2)
+
+
+def test_decode_append_attention_rejects_bad_input():
+    Q = torch.randn(1, 8, 1, 128, device="cuda").bfloat16()
+    kb = torch.zeros(1, 4, 16, 128, device="cuda").bfloat16()
+    kn = torch.zeros(1, 4, 1, 128, device="cuda").bfloat16()
+    with pytest.raises(ValueError):
+        ops.decode_append_attention(Q, kn, kn, kb, kb, 16)    # no room for the row
+    with pytest.raises(ValueError):
+        ops.decode_append_attention(Q, kn, kn, kb, kb, -1)
+    with pytest.raises(TypeError):
+        ops.decode_append_attention(Q, kn.half(), kn.half(), kb, kb, 3)
