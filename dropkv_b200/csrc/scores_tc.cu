@@ -878,73 +878,69 @@ __global__ void __launch_bounds__(NTH, 1)
         if (ne > 0) {
           const int m_lo = e0 / D, nrow = (e1 - 1) / D - m_lo + 1;
           const int nst = nrow * a.gs;
-          // partial maxima and sums of the slice's rows, all loads in flight together
-          for (int k0 = 0; k0 < 2 * nst; k0 += 4 * NEPI) {
-            float val[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int k = k0 + u * NEPI + et;
-              val[u] = 0.f;
-              if (k < nst) {
-                const int r = k / a.gs, c = k % a.gs;
-                val[u] = __ldcg(a.part_m + (hb + c) * M + m_lo + r);
-              } else if (k < 2 * nst) {
-                const int kk = k - nst, r = kk / a.gs, c = kk % a.gs;
-                val[u] = __ldcg(a.part_s + (hb + c) * M + m_lo + r);
-              }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int k = k0 + u * NEPI + et;
-              if (k < nst) wts[k] = val[u];
-              else if (k < 2 * nst) sts[k - nst] = val[u];
-            }
-          }
-          epi_sync();
-          for (int r = warp; r < nrow; r += NEW) {
-            float mxr = -INFINITY;
-            for (int c = lane; c < a.gs; c += 32) mxr = fmaxf(mxr, wts[r * a.gs + c]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mxr = fmaxf(mxr, __shfl_xor_sync(0xffffffffu, mxr, o));
-            float tot = 0.f;
-            for (int c = lane; c < a.gs; c += 32) {
-              const float pm = wts[r * a.gs + c];
-              const float w = (pm == -INFINITY) ? 0.f : exp2f(pm - mxr);
-              wts[r * a.gs + c] = w;
-              tot = fmaf(w, sts[r * a.gs + c], tot);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-            if (lane == 0) {
-              red[r] = tot;
-              red[NPAD + r] = mxr;
-            }
-          }
-          epi_sync();
-          // weighted sums in chunks of elements whose partials fit the P tiles
+          // weighted sums in chunks of elements whose partials fit the P tiles; the
+          // first chunk's loads go out together with the rows' partial maxima and
+          // sums (one L2 round trip for the whole slice when it fits one chunk)
           const int ec = max(1, min(ne, CAP / a.gs));
           for (int cs = 0; cs < ne; cs += ec) {
             const int cn = min(ec, ne - cs);
             const int npairs = a.gs * cn;
-            for (int k0 = 0; k0 < npairs; k0 += 8 * NEPI) {
-              float val[8];
+            // the rows' partial maxima and sums (first chunk; one per thread at most)
+            float msv = 0.f;
+            const bool ms = cs == 0 && et < 2 * nst;
+            if (ms) {
+              const int kk = et < nst ? et : et - nst;
+              const int r = kk / a.gs, c = kk - r * a.gs;
+              msv = __ldcg((et < nst ? a.part_m : a.part_s) + (hb + c) * M + m_lo + r);
+            }
+            // pair k = c cn + e (partial c, element e), stepped by NEPI without divisions
+            const int dq = NEPI / cn, dr = NEPI - dq * cn;
+            int c = et / cn, e = et - (et / cn) * cn;
+            for (int k0 = 0; k0 < npairs; k0 += 16 * NEPI) {
+              float val[16];
 #pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                const int k = k0 + u * NEPI + et;
-                val[u] = 0.f;
-                if (k < npairs) {
-                  const int c = k / cn, e = k % cn;
-                  const int eg = e0 + cs + e, m = eg / D, d = eg % D;
-                  val[u] = __ldcg(a.part_y + ((hb + c) * M + m) * D + d);
+              for (int u = 0; u < 16; ++u) {
+                val[u] = c < a.gs ? __ldcg(a.part_y + (hb + c) * E + e0 + cs + e) : 0.f;
+                c += dq;
+                e += dr;
+                if (e >= cn) {
+                  e -= cn;
+                  ++c;
                 }
               }
 #pragma unroll
-              for (int u = 0; u < 8; ++u) {
+              for (int u = 0; u < 16; ++u) {
                 const int k = k0 + u * NEPI + et;
                 if (k < npairs) acc[k] = val[u];
               }
             }
+            if (ms) {
+              if (et < nst) wts[et] = msv;
+              else sts[et - nst] = msv;
+            }
             epi_sync();
+            if (cs == 0) {  // the rows' maxima and the weights of the partials
+              for (int r = warp; r < nrow; r += NEW) {
+                float mxr = -INFINITY;
+                for (int c = lane; c < a.gs; c += 32) mxr = fmaxf(mxr, wts[r * a.gs + c]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mxr = fmaxf(mxr, __shfl_xor_sync(0xffffffffu, mxr, o));
+                float tot = 0.f;
+                for (int c = lane; c < a.gs; c += 32) {
+                  const float pm = wts[r * a.gs + c];
+                  const float w = (pm == -INFINITY) ? 0.f : exp2f(pm - mxr);
+                  wts[r * a.gs + c] = w;
+                  tot = fmaf(w, sts[r * a.gs + c], tot);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+                if (lane == 0) {
+                  red[r] = tot;
+                  red[NPAD + r] = mxr;
+                }
+              }
+              epi_sync();
+            }
             // SPL threads per element, each over a fixed subset of the partials
             const int spl = max(1, min(8, NEPI / cn));
             for (int idx = et; idx < cn * spl; idx += NEPI) {
