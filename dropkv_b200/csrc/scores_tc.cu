@@ -885,13 +885,20 @@ __global__ void __launch_bounds__(NTH, 1)
           for (int cs = 0; cs < ne; cs += ec) {
             const int cn = min(ec, ne - cs);
             const int npairs = a.gs * cn;
-            // the rows' partial maxima and sums (first chunk; one per thread at most)
-            float msv = 0.f;
-            const bool ms = cs == 0 && et < 2 * nst;
-            if (ms) {
-              const int kk = et < nst ? et : et - nst;
-              const int r = kk / a.gs, c = kk - r * a.gs;
-              msv = __ldcg((et < nst ? a.part_m : a.part_s) + (hb + c) * M + m_lo + r);
+            // the rows' partial maxima and sums (first chunk only): 2 nst values,
+            // nst = nrow gs <= M + 2 gs, so two per thread cover the plans of a
+            // 148-SM GPU (M <= 64); a loop takes any rest
+            const int nms = cs == 0 ? 2 * nst : 0;
+            float msv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int k = et + u * NEPI;
+              msv[u] = 0.f;
+              if (k < nms) {
+                const int kk = k < nst ? k : k - nst;
+                const int r = kk / a.gs, c = kk - r * a.gs;
+                msv[u] = __ldcg((k < nst ? a.part_m : a.part_s) + (hb + c) * M + m_lo + r);
+              }
             }
             // pair k = c cn + e (partial c, element e), stepped by NEPI without divisions
             const int dq = NEPI / cn, dr = NEPI - dq * cn;
@@ -914,9 +921,18 @@ __global__ void __launch_bounds__(NTH, 1)
                 if (k < npairs) acc[k] = val[u];
               }
             }
-            if (ms) {
-              if (et < nst) wts[et] = msv;
-              else sts[et - nst] = msv;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int k = et + u * NEPI;
+              if (k < nst) wts[k] = msv[u];
+              else if (k < nms) sts[k - nst] = msv[u];
+            }
+            for (int k = et + 2 * NEPI; k < nms; k += NEPI) {
+              const int kk = k < nst ? k : k - nst;
+              const int r = kk / a.gs, c = kk - r * a.gs;
+              const float x = __ldcg((k < nst ? a.part_m : a.part_s) + (hb + c) * M + m_lo + r);
+              if (k < nst) wts[k] = x;
+              else sts[k - nst] = x;
             }
             epi_sync();
             if (cs == 0) {  // the rows' maxima and the weights of the partials
