@@ -169,6 +169,11 @@ __global__ void __launch_bounds__(DA_NT, 1) decode_attn_kernel(DaArgs a) {
   // rows from pos on: the new rows (not yet in the buffers)
   const T* knb = reinterpret_cast<const T*>(a.k_new) + b * a.new_sb + hkv * a.new_sh - (int64_t)a.pos * D;
   const T* vnb = reinterpret_cast<const T*>(a.v_new) + b * a.new_sb + hkv * a.new_sh - (int64_t)a.pos * D;
+  // launched with programmatic dependent launch: every global access below waits
+  // for the kernel before this one (it may write Q, the new rows or reuse the
+  // workspace); the next kernel may be scheduled as this one's CTAs exit
+  pdl_launch_dependents();
+  pdl_wait();
   if (a.pos < a.L && split == 0 && tile == 0) {  // append the new rows to the buffers (read from the inputs here)
     const int nvec = (a.L - a.pos) * D / 8;
     uint4* kd = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.k_buf) + b * a.kv_sb + hkv * a.kv_sh + (int64_t)a.pos * D);
@@ -524,6 +529,11 @@ int launch_decode_attention(const void* q, int64_t q_sb, int64_t q_sh, int64_t q
   cfg.blockDim = dim3(DA_NT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // may start as the previous kernel ends
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
   if (e != cudaSuccess) return fail(DROPKV_ERR_CUDA, "decode attention launch: %s", cudaGetErrorString(e));
   return check_launch("decode_attention");
