@@ -850,8 +850,9 @@ __global__ void __launch_bounds__(NTH, 1)
       auto group_barrier = [&](int* ctr) {
         epi_sync();
         if (et == 0 && !*vabort) {
-          __threadfence();
-          atomicAdd(ctr, 1);
+          // release: the epilogue's stores before the named barrier (partials,
+          // merged y) are visible to every CTA that acquires the count
+          asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(ctr) : "memory");
           const uint64_t t_start = tc::globaltimer_ns();
           while (true) {
             int v;
@@ -860,9 +861,8 @@ __global__ void __launch_bounds__(NTH, 1)
             if (*vabort) break;
             if (tc::globaltimer_ns() - t_start > a.wait_ns) { fail_wait(35); break; }
           }
-          __threadfence();
         }
-        epi_sync();
+        epi_sync();  // orders the other threads' loads after the acquire
       };
       group_barrier(a.ctr + 2 * h);
       stamp(rd, TR_BAR_A);
