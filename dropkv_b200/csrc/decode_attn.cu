@@ -363,12 +363,17 @@ __global__ void __launch_bounds__(DA_NT, 1) decode_attn_kernel(DaArgs a) {
     pp[tid * PR + D + 1] = rsum[tid];
   }
   // ---- the last CTA of the tile merges every partial ---------------------------
-  __threadfence();  // this CTA's partial is visible before its arrival is counted
+  // the arrival is an acquire-release add: it publishes this CTA's partial (its
+  // threads' stores come before it through the barrier) and, in the last CTA,
+  // acquires every other CTA's; the barrier after it orders this CTA's loads
   __syncthreads();
-  if (tid == 0) *last_cta = atomicAdd(&a.counter[tile_id], 1u) == (unsigned)(a.splits - 1);
+  if (tid == 0) {
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&a.counter[tile_id]) : "memory");
+    *last_cta = prev == (unsigned)(a.splits - 1);
+  }
   __syncthreads();
   if (!*last_cta) return;
-  __threadfence();
   const float* pt = a.part + (size_t)tile_id * a.splits * DA_ROWS * PR;
   // (a) every partial's max and sum into shared memory
   for (int i = tid; i < a.splits * mvalid; i += DA_NT) {
