@@ -868,9 +868,12 @@ __global__ void __launch_bounds__(NTH, 1)
       stamp(rd, TR_BAR_A);
       {
         // This CTA merges elements [e0, e1) of the head's M x D y with the
-        // max-rescale rule (dropkv_triton.py:441-452), in a fixed order.
+        // max-rescale rule (dropkv_triton.py:441-452), in a fixed order. The
+        // slices start on multiples of 4 elements (E = M D is one), so the
+        // partials are read as 16-byte vectors.
         const int E = M * D;
-        const int e0 = (int)(((long long)rank * E) / a.gs), e1 = (int)(((long long)(rank + 1) * E) / a.gs);
+        const int e0 = (int)((((long long)rank * E) / a.gs) & ~3LL);
+        const int e1 = (int)((((long long)(rank + 1) * E) / a.gs) & ~3LL);
         const int ne = e1 - e0;
         const size_t hb = (size_t)h * a.gs;
         float* acc = reinterpret_cast<float*>(sm + L::PS);  // P tiles are idle here
@@ -881,10 +884,9 @@ __global__ void __launch_bounds__(NTH, 1)
           // weighted sums in chunks of elements whose partials fit the P tiles; the
           // first chunk's loads go out together with the rows' partial maxima and
           // sums (one L2 round trip for the whole slice when it fits one chunk)
-          const int ec = max(1, min(ne, CAP / a.gs));
+          const int ec = max(4, min(ne, (CAP / a.gs) & ~3));  // a multiple of 4, as ne is
           for (int cs = 0; cs < ne; cs += ec) {
             const int cn = min(ec, ne - cs);
-            const int npairs = a.gs * cn;
             // the rows' partial maxima and sums (first chunk only): 2 nst values,
             // nst = nrow gs <= M + 2 gs, so two per thread cover the plans of a
             // 148-SM GPU (M <= 64); a loop takes any rest
@@ -900,25 +902,28 @@ __global__ void __launch_bounds__(NTH, 1)
                 msv[u] = __ldcg((k < nst ? a.part_m : a.part_s) + (hb + c) * M + m_lo + r);
               }
             }
-            // pair k = c cn + e (partial c, element e), stepped by NEPI without divisions
-            const int dq = NEPI / cn, dr = NEPI - dq * cn;
-            int c = et / cn, e = et - (et / cn) * cn;
-            for (int k0 = 0; k0 < npairs; k0 += 16 * NEPI) {
-              float val[16];
+            // vector k = c cn4 + e (partial c, elements 4e .. 4e + 3 of the chunk),
+            // stepped by NEPI without divisions; it lands at acc[4k] = acc[c cn + 4e]
+            const int cn4 = cn / 4, npairs4 = a.gs * cn4;
+            const int dq = NEPI / cn4, dr = NEPI - dq * cn4;
+            int c = et / cn4, e = et - (et / cn4) * cn4;
+            for (int k0 = 0; k0 < npairs4; k0 += 4 * NEPI) {
+              float4 val[4];
 #pragma unroll
-              for (int u = 0; u < 16; ++u) {
-                val[u] = c < a.gs ? __ldcg(a.part_y + (hb + c) * E + e0 + cs + e) : 0.f;
+              for (int u = 0; u < 4; ++u) {
+                val[u] = c < a.gs ? __ldcg(reinterpret_cast<const float4*>(a.part_y + (hb + c) * E + e0 + cs) + e)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
                 c += dq;
                 e += dr;
-                if (e >= cn) {
-                  e -= cn;
+                if (e >= cn4) {
+                  e -= cn4;
                   ++c;
                 }
               }
 #pragma unroll
-              for (int u = 0; u < 16; ++u) {
+              for (int u = 0; u < 4; ++u) {
                 const int k = k0 + u * NEPI + et;
-                if (k < npairs) acc[k] = val[u];
+                if (k < npairs4) reinterpret_cast<float4*>(acc)[k] = val[u];
               }
             }
 #pragma unroll
